@@ -1,0 +1,196 @@
+/*
+ * kbb200.h — C ABI of the B200 (sm_100a) fp32 operator library.
+ *
+ * One shared library (libkbb200.so) exports every entry point below as plain
+ * `extern "C"` functions: device pointers, element counts and a CUDA stream,
+ * no torch types.  Each entry replaces the compiled entry of one candidate of
+ * the reference operator library (candidates/<problem>/v*.py, whose C++ entry
+ * took torch::Tensor arguments and launched on the current stream).
+ *
+ * Conventions (all entries):
+ *   - Pointers are device pointers to contiguous fp32 data unless stated.
+ *   - Launches are asynchronous on `stream` (NULL = legacy default stream).
+ *   - Inputs are never written.  Outputs are fully overwritten.
+ *   - Entries never allocate device memory.  Entries that need scratch take
+ *     (workspace, workspace_bytes); query the size with the matching
+ *     *_workspace_size() call.  Workspace need not be initialised.
+ *   - Return KB_OK (0) or a kbStatus code; kb_last_error() describes the most
+ *     recent failure on the calling thread.
+ *   - Empty inputs (n == 0, rows == 0, ...) are valid and launch nothing,
+ *     except reductions to a scalar, which write their identity result.
+ */
+#ifndef KBB200_H
+#define KBB200_H
+
+#include <stddef.h>
+#include <stdint.h>
+
+#if defined(__GNUC__)
+#define KB_API __attribute__((visibility("default")))
+#else
+#define KB_API
+#endif
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+typedef struct CUstream_st* kbStream; /* same handle type as cudaStream_t */
+
+typedef enum kbStatus {
+  KB_OK = 0,
+  KB_ERR_INVALID_ARG = 1,   /* bad size, null pointer, misaligned scratch */
+  KB_ERR_UNSUPPORTED = 2,   /* shape outside the kernel's contract */
+  KB_ERR_WORKSPACE = 3,     /* workspace missing or smaller than required */
+  KB_ERR_CUDA = 4,          /* CUDA runtime error (launch / attribute) */
+  KB_ERR_DEVICE = 5         /* device is not sm_100 class */
+} kbStatus;
+
+/* ---- library / diagnostics ------------------------------------------- */
+KB_API int kb_version(void);                 /* MAJOR*10000 + MINOR*100 + PATCH */
+KB_API const char* kb_status_string(int status);
+KB_API const char* kb_last_error(void);      /* thread-local, never NULL */
+KB_API int kb_device_sm_count(int device);   /* streaming multiprocessors, or -1 */
+
+/* ---- elementwise (y = f(x), n elements) ------------------------------- */
+/* replaces mingpt_gelu_entry, candidates/88_MinGPTNewGelu/v1.py:21-26
+ * y = 0.5 x (1 + tanh(sqrt(2/pi) (x + 0.044715 x^3)))                      */
+KB_API int kb_gelu_tanh_f32(const float* x, float* y, int64_t n, kbStream stream);
+/* replaces gelu_entry, candidates/26_GELU_/v1.py:18-23 (exact erf form)    */
+KB_API int kb_gelu_erf_f32(const float* x, float* y, int64_t n, kbStream stream);
+/* replaces swish_entry, candidates/25_Swish/v1.py:18-23: y = x sigmoid(x)  */
+KB_API int kb_swish_f32(const float* x, float* y, int64_t n, kbStream stream);
+/* replaces relu_entry, candidates/19_ReLU/v1.py:15-20: y = max(x, 0)       */
+KB_API int kb_relu_f32(const float* x, float* y, int64_t n, kbStream stream);
+
+/* ---- row normalisation over the last `cols` elements of each row ------ */
+/* replaces layernorm_entry, candidates/40_LayerNorm/v1.py:62-80.
+ * gamma/beta may be NULL (identity affine).  Biased variance, eps inside
+ * the square root, as torch.nn.functional.layer_norm.                      */
+KB_API int kb_layernorm_f32(const float* x, const float* gamma, const float* beta,
+                     float* y, int64_t rows, int64_t cols, float eps,
+                     kbStream stream);
+/* replaces rmsnorm_entry, candidates/36_RMSNorm_/v3.py:42-51.
+ * x is viewed as [outer, features, inner]; each (outer, inner) position is
+ * normalised over `features`: y = x / sqrt(mean(x^2) + eps) * gamma[f].
+ * inner == 1 is the last-dim form; inner > 1 the channel (dim 1) form.
+ * gamma may be NULL.                                                      */
+KB_API int kb_rmsnorm_f32(const float* x, const float* gamma, float* y,
+                   int64_t outer, int64_t features, int64_t inner, float eps,
+                   kbStream stream);
+/* replaces softmax_entry, candidates/23_Softmax/v1.py:47-52 (last dim)     */
+KB_API int kb_softmax_f32(const float* x, float* y, int64_t rows, int64_t cols,
+                   kbStream stream);
+/* replaces logsoftmax_entry, candidates/24_LogSoftmax/v1.py:46-51          */
+KB_API int kb_logsoftmax_f32(const float* x, float* y, int64_t rows, int64_t cols,
+                      kbStream stream);
+
+/* ---- reductions over dim 1 of x[B, I, J] ------------------------------ */
+/* replaces colreduce_entry, candidates/47_Sum_reduction_over_a_dimension/
+ * v1.py:28-35: out[b, j] = sum_i x[b, i, j]                                */
+KB_API int kb_sum_dim1_f32(const float* x, float* out, int64_t B, int64_t I,
+                    int64_t J, kbStream stream);
+/* replaces colreduce_mean_entry, candidates/48_Mean_reduction_over_a_
+ * dimension/v1.py:25-32: out[b, j] = sum_i x[b, i, j] / I                  */
+KB_API int kb_mean_dim1_f32(const float* x, float* out, int64_t B, int64_t I,
+                     int64_t J, kbStream stream);
+/* replaces argmax_entry, candidates/51_Argmax_over_a_dimension/v1.py:27-31.
+ * out[b, j] = lowest i attaining the maximum; NaN counts as the maximum
+ * (torch.argmax).  out is int64.                                          */
+KB_API int kb_argmax_dim1_f32(const float* x, int64_t* out, int64_t B, int64_t I,
+                       int64_t J, kbStream stream);
+
+/* ---- global reductions ------------------------------------------------ */
+/* replaces mse_entry, candidates/94_MSELoss/v1.py:35-45:
+ * out[0] = mean((a - b)^2) over n elements (deterministic order).          */
+KB_API size_t kb_mse_workspace_size(int64_t n);
+KB_API int kb_mse_f32(const float* a, const float* b, float* out, int64_t n,
+               void* workspace, size_t workspace_bytes, kbStream stream);
+/* sharded form: partial[0] = sum((a - b)^2) over this shard, in fp64, so a
+ * collective can add shards before kb_mse_finalize_f32 divides by the total
+ * element count.                                                          */
+KB_API int kb_mse_partial_f64(const float* a, const float* b, double* partial,
+                       int64_t n, void* workspace, size_t workspace_bytes,
+                       kbStream stream);
+KB_API int kb_mse_finalize_f32(const double* total, float* out, int64_t total_n,
+                        kbStream stream);
+
+/* replaces frobenius_entry, candidates/37_FrobeniusNorm_/v1.py:48-58:
+ * y = x / ||x||_F over all n elements.                                    */
+KB_API size_t kb_frobenius_workspace_size(int64_t n);
+KB_API int kb_frobenius_normalize_f32(const float* x, float* y, int64_t n,
+                               void* workspace, size_t workspace_bytes,
+                               kbStream stream);
+/* sharded form: sumsq[0] = sum(x^2) over this shard (fp64), then
+ * y = x / sqrt(total) once a collective has summed the shards.            */
+KB_API int kb_sumsq_partial_f64(const float* x, double* sumsq, int64_t n,
+                         void* workspace, size_t workspace_bytes,
+                         kbStream stream);
+KB_API int kb_scale_by_inv_norm_f32(const float* x, float* y, int64_t n,
+                             const double* total_sumsq, kbStream stream);
+
+/* ---- spatial ---------------------------------------------------------- */
+/* replaces maxpool_entry, candidates/42_Max_Pooling_2D/v1.py:37-44, with
+ * stride and dilation honoured (the reference kernel ignored both).
+ * NCHW; padding is -inf; NaN propagates as in torch.max_pool2d.            */
+KB_API int kb_maxpool2d_f32(const float* x, float* y, int64_t N, int64_t C,
+                     int64_t H, int64_t W, int64_t OH, int64_t OW,
+                     int kernel, int stride, int pad, int dilation,
+                     kbStream stream);
+
+/* replaces bn_entry, candidates/33_BatchNorm/v1.py:53-68: training-mode
+ * BatchNorm2d over NCHW x with batch statistics (biased variance).
+ * gamma/beta may be NULL.  running_mean/running_var may be NULL; when given
+ * they are updated in place with `momentum` and the unbiased variance,
+ * as torch.nn.BatchNorm2d does in training mode.                          */
+KB_API size_t kb_batchnorm_workspace_size(int64_t N, int64_t C, int64_t HW);
+KB_API int kb_batchnorm_train_f32(const float* x, const float* gamma,
+                           const float* beta, float* y, int64_t N, int64_t C,
+                           int64_t HW, float eps, float momentum,
+                           float* running_mean, float* running_var,
+                           void* workspace, size_t workspace_bytes,
+                           kbStream stream);
+/* sharded form: stats[0:C] = per-channel sum, stats[C:2C] = per-channel sum
+ * of squares over this shard (fp64); a collective adds them across shards,
+ * then kb_batchnorm_apply_f32 normalises with `total_count` elements per
+ * channel.                                                                */
+KB_API int kb_batchnorm_stats_f64(const float* x, double* stats, int64_t N,
+                           int64_t C, int64_t HW, void* workspace,
+                           size_t workspace_bytes, kbStream stream);
+KB_API int kb_batchnorm_apply_f32(const float* x, const float* gamma,
+                           const float* beta, float* y, const double* stats,
+                           int64_t N, int64_t C, int64_t HW,
+                           int64_t total_count, float eps, float momentum,
+                           float* running_mean, float* running_var,
+                           kbStream stream);
+
+/* ---- dense contractions ----------------------------------------------- */
+/* replaces sgemm_entry, candidates/1_Square_matrix_multiplication_/
+ * v1.py:83-102: C[M,N] = op(A) B with op(A) = A[M,K] (trans_a = 0) or
+ * A[K,M]^T (trans_a = 1); B[K,N]; row-major with leading dimensions.
+ * 3xTF32 on tcgen05 tensor cores: fp32-level accuracy.                     */
+KB_API int kb_sgemm_3xtf32(const float* A, const float* B, float* C, int64_t M,
+                    int64_t N, int64_t K, int64_t lda, int64_t ldb,
+                    int64_t ldc, int trans_a, kbStream stream);
+/* replaces sgemm_entry batched mode, candidates/3_Batched_matrix_
+ * multiplication/v1.py:83-102 (with C's row stride = N, fixing the ldc
+ * bug there): C[b] = A[b] B[b] for contiguous A[batch,M,K], B[batch,K,N].  */
+KB_API int kb_bgemm_3xtf32(const float* A, const float* B, float* C, int64_t batch,
+                    int64_t M, int64_t N, int64_t K, kbStream stream);
+/* replaces splitk_gemm_entry, candidates/6_Matmul_with_large_K_dimension_/
+ * v1.py:67-78: C[M,N] = A[M,K] B[K,N] with K split across the SMs and a
+ * deterministic reduction of the partial tiles (no atomics).               */
+KB_API size_t kb_gemm_splitk_workspace_size(int64_t M, int64_t N, int64_t K);
+KB_API int kb_gemm_splitk_3xtf32(const float* A, const float* B, float* C,
+                          int64_t M, int64_t N, int64_t K, void* workspace,
+                          size_t workspace_bytes, kbStream stream);
+/* replaces gemv_entry, candidates/4_Matrix_vector_multiplication_/
+ * v1.py:36-43: y[M] = A[M,K] x[K] (deterministic, no atomics).            */
+KB_API int kb_gemv_f32(const float* A, const float* x, float* y, int64_t M,
+                int64_t K, kbStream stream);
+
+#ifdef __cplusplus
+}
+#endif
+
+#endif /* KBB200_H */

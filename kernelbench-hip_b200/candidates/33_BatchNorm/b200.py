@@ -1,0 +1,25 @@
+# 33_BatchNorm on B200 — training-mode BatchNorm2d with affine, no atomics
+# Drop-in for candidates/33_BatchNorm/v1.py: same ENTRY / Model contract, compiled entry
+# served by libkbb200.so (sm_100a) through kbb200.ext.
+ENTRY = "bn_entry"
+
+import torch
+
+import kbb200.ext as EXT
+
+
+class Model(torch.nn.Module):
+    def __init__(self, num_features: int = 128, eps: float = 1e-5, momentum: float = 0.1):
+        super().__init__()
+        self.eps, self.momentum = eps, momentum
+        self.register_buffer("running_mean", torch.zeros(num_features))
+        self.register_buffer("running_var", torch.ones(num_features))
+
+    def forward(self, x, weight, bias):
+        y = torch.empty_like(x)
+        EXT.bn_entry(x, y, weight, bias, self.eps, self.momentum, self.running_mean,
+                     self.running_var)
+        return y
+
+
+ModelNew = Model

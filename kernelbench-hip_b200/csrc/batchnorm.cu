@@ -1,0 +1,240 @@
+// batchnorm.cu — training-mode BatchNorm2d over NCHW fp32 (batch statistics,
+// biased variance for normalisation, optional running-statistics update).
+//
+// Pass 1 (stats): grid (C, S).  CTA (c, s) streams the (n, c) planes of its
+// batch slice — each plane is HW contiguous floats — and writes one fp64
+// (sum, sum of squares) pair to the workspace.  No atomics (the reference's
+// per-256-element atomics ran at 41 GB/s, candidates/33_BatchNorm/v1.py:36-40).
+// Pass 2 (apply): one CTA per (n, c) plane folds the S partials of its channel
+// in a fixed order (or reads fp64 totals produced by a cross-GPU collective),
+// derives mean / inv-std in fp64 and writes y = (x - mean) * (inv_std * gamma)
+// + beta.  x is read twice (2 GiB does not fit on chip); planes are applied in
+// reverse order so the first ones still sit in L2 from the end of pass 1.
+#include "kb_common.cuh"
+
+namespace kb {
+namespace {
+
+constexpr int kThreads = 256;
+constexpr int kUnroll = 4;
+
+struct BnShape {
+  int64_t N, C, HW;
+};
+
+int bn_splits(int64_t N, int64_t C) {
+  const int64_t want = ceil_div((int64_t)sm_count() * 4, std::max<int64_t>(C, 1));
+  return (int)std::max<int64_t>(1, std::min<int64_t>(N, want));
+}
+
+// per-thread fp32 sums over one plane, promoted to fp64 per 16-element tile
+__device__ __forceinline__ void plane_sums(const float* __restrict__ p, int64_t HW, bool vec,
+                                           double& s1, double& s2) {
+  int64_t scalar_begin = 0;
+  if (vec) {
+    const float4* p4 = reinterpret_cast<const float4*>(p);
+    const int64_t nvec = HW / 4;
+    const int64_t tile = (int64_t)kThreads * kUnroll;
+    int64_t i = threadIdx.x;
+    for (; i + (kUnroll - 1) * kThreads < nvec; i += tile) {
+      float4 v[kUnroll];
+#pragma unroll
+      for (int u = 0; u < kUnroll; ++u) v[u] = __ldg(p4 + i + u * kThreads);
+      float a = 0.f, q = 0.f;
+#pragma unroll
+      for (int u = 0; u < kUnroll; ++u) {
+        a += (v[u].x + v[u].y) + (v[u].z + v[u].w);
+        q += (v[u].x * v[u].x + v[u].y * v[u].y) + (v[u].z * v[u].z + v[u].w * v[u].w);
+      }
+      s1 += (double)a;
+      s2 += (double)q;
+    }
+    for (; i < nvec; i += kThreads) {
+      const float4 v = __ldg(p4 + i);
+      s1 += (double)((v.x + v.y) + (v.z + v.w));
+      s2 += (double)((v.x * v.x + v.y * v.y) + (v.z * v.z + v.w * v.w));
+    }
+    scalar_begin = nvec * 4;
+  }
+  for (int64_t i = scalar_begin + threadIdx.x; i < HW; i += kThreads) {
+    const float v = p[i];
+    s1 += (double)v;
+    s2 += (double)(v * v);
+  }
+}
+
+__global__ void __launch_bounds__(kThreads)
+bn_stats_kernel(const float* __restrict__ x, BnShape sh, int S, bool vec,
+                double2* __restrict__ partials) {
+  __shared__ double red[32];
+  const int64_t c = blockIdx.x;
+  const int s = blockIdx.y;
+  const int64_t n0 = sh.N * s / S, n1 = sh.N * (s + 1) / S;
+  double s1 = 0.0, s2 = 0.0;
+  for (int64_t n = n0; n < n1; ++n) plane_sums(x + (n * sh.C + c) * sh.HW, sh.HW, vec, s1, s2);
+  s1 = block_sum<kThreads>(s1, red);
+  s2 = block_sum<kThreads>(s2, red);
+  if (threadIdx.x == 0) partials[c * S + s] = make_double2(s1, s2);
+}
+
+// totals: stats[c] = sum, stats[C + c] = sum of squares (fp64)
+__global__ void bn_fold_kernel(const double2* __restrict__ partials, int64_t C, int S,
+                               double* __restrict__ stats) {
+  const int64_t c = (int64_t)blockIdx.x * blockDim.x + threadIdx.x;
+  if (c >= C) return;
+  double s1 = 0.0, s2 = 0.0;
+  for (int s = 0; s < S; ++s) {
+    const double2 p = partials[c * S + s];
+    s1 += p.x;
+    s2 += p.y;
+  }
+  stats[c] = s1;
+  stats[C + c] = s2;
+}
+
+// One CTA per (n, c) plane, planes visited in reverse order.  Channel totals
+// come from `partials` (S > 0, fixed-order fold) or from `stats` (S == 0).
+__global__ void __launch_bounds__(kThreads)
+bn_apply_kernel(const float* __restrict__ x, const float* __restrict__ gamma,
+                const float* __restrict__ beta, float* __restrict__ y, BnShape sh,
+                const double2* __restrict__ partials, int S, const double* __restrict__ stats,
+                int64_t count, float eps, float momentum, float* running_mean,
+                float* running_var, bool vec) {
+  const int64_t plane = sh.N * sh.C - 1 - (int64_t)blockIdx.x;
+  const int64_t n = plane / sh.C, c = plane - n * sh.C;
+  double s1 = 0.0, s2 = 0.0;
+  if (S > 0) {
+    for (int s = 0; s < S; ++s) {
+      const double2 p = partials[c * S + s];
+      s1 += p.x;
+      s2 += p.y;
+    }
+  } else {
+    s1 = stats[c];
+    s2 = stats[sh.C + c];
+  }
+  const double mean_d = s1 / (double)count;
+  const double var_d = fmax(s2 / (double)count - mean_d * mean_d, 0.0);
+  const float mean = (float)mean_d;
+  const float inv_std = (float)(1.0 / sqrt(var_d + (double)eps));
+  const float scale = inv_std * (gamma ? gamma[c] : 1.0f);
+  const float shift = beta ? beta[c] : 0.0f;
+  if (n == 0 && threadIdx.x == 0 && running_mean && running_var) {
+    const double unbiased = count > 1 ? var_d * (double)count / (double)(count - 1) : var_d;
+    running_mean[c] = (1.0f - momentum) * running_mean[c] + momentum * mean;
+    running_var[c] = (1.0f - momentum) * running_var[c] + momentum * (float)unbiased;
+  }
+  const float* xp = x + plane * sh.HW;
+  float* yp = y + plane * sh.HW;
+  int64_t scalar_begin = 0;
+  if (vec) {
+    const float4* x4 = reinterpret_cast<const float4*>(xp);
+    float4* y4 = reinterpret_cast<float4*>(yp);
+    const int64_t nvec = sh.HW / 4;
+    const int64_t tile = (int64_t)kThreads * kUnroll;
+    int64_t i = threadIdx.x;
+    for (; i + (kUnroll - 1) * kThreads < nvec; i += tile) {
+      float4 v[kUnroll];
+#pragma unroll
+      for (int u = 0; u < kUnroll; ++u) v[u] = ld_stream(x4 + i + u * kThreads);
+#pragma unroll
+      for (int u = 0; u < kUnroll; ++u)
+        st_stream(y4 + i + u * kThreads,
+                  make_float4((v[u].x - mean) * scale + shift, (v[u].y - mean) * scale + shift,
+                              (v[u].z - mean) * scale + shift, (v[u].w - mean) * scale + shift));
+    }
+    for (; i < nvec; i += kThreads) {
+      const float4 v = ld_stream(x4 + i);
+      st_stream(y4 + i, make_float4((v.x - mean) * scale + shift, (v.y - mean) * scale + shift,
+                                    (v.z - mean) * scale + shift, (v.w - mean) * scale + shift));
+    }
+    scalar_begin = nvec * 4;
+  }
+  for (int64_t i = scalar_begin + threadIdx.x; i < sh.HW; i += kThreads)
+    yp[i] = (xp[i] - mean) * scale + shift;
+}
+
+int bn_check(const char* name, const float* x, int64_t N, int64_t C, int64_t HW) {
+  KB_REQUIRE(N >= 0 && C >= 0 && HW >= 0, KB_ERR_INVALID_ARG, "%s: negative size", name);
+  KB_REQUIRE(x || N * C * HW == 0, KB_ERR_INVALID_ARG, "%s: null input", name);
+  KB_REQUIRE(C <= 0x7fffffff && N * C <= 0x7fffffff, KB_ERR_UNSUPPORTED, "%s: too many planes", name);
+  return KB_OK;
+}
+
+}  // namespace
+}  // namespace kb
+
+extern "C" {
+
+size_t kb_batchnorm_workspace_size(int64_t N, int64_t C, int64_t) {
+  // worst case S = min(N, SMs * 4 / C) with SMs <= 160
+  const int64_t S = std::max<int64_t>(1, std::min<int64_t>(N, kb::ceil_div(160 * 4, std::max<int64_t>(C, 1))));
+  return (size_t)(C * S) * sizeof(double2) + 256;
+}
+
+int kb_batchnorm_train_f32(const float* x, const float* gamma, const float* beta, float* y,
+                           int64_t N, int64_t C, int64_t HW, float eps, float momentum,
+                           float* running_mean, float* running_var, void* workspace,
+                           size_t workspace_bytes, kbStream stream) {
+  const char* name = "kb_batchnorm_train_f32";
+  if (int st = kb::bn_check(name, x, N, C, HW)) return st;
+  if (N * C * HW == 0) return KB_OK;
+  KB_REQUIRE(y, KB_ERR_INVALID_ARG, "%s: null output", name);
+  KB_REQUIRE(workspace && workspace_bytes >= kb_batchnorm_workspace_size(N, C, HW),
+             KB_ERR_WORKSPACE, "%s: workspace of %zu bytes needed", name,
+             kb_batchnorm_workspace_size(N, C, HW));
+  KB_REQUIRE((reinterpret_cast<uintptr_t>(workspace) & 15) == 0, KB_ERR_INVALID_ARG,
+             "%s: workspace must be 16-byte aligned", name);
+  const int S = kb::bn_splits(N, C);
+  const bool vec = HW % 4 == 0 && kb::aligned16(x) && kb::aligned16(y);
+  double2* parts = static_cast<double2*>(workspace);
+  kb::BnShape sh{N, C, HW};
+  kb::bn_stats_kernel<<<dim3((unsigned)C, (unsigned)S), kb::kThreads, 0, stream>>>(x, sh, S, vec, parts);
+  if (int st = kb::check_launch(name)) return st;
+  kb::bn_apply_kernel<<<(unsigned)(N * C), kb::kThreads, 0, stream>>>(
+      x, gamma, beta, y, sh, parts, S, nullptr, N * HW, eps, momentum, running_mean, running_var, vec);
+  return kb::check_launch(name);
+}
+
+int kb_batchnorm_stats_f64(const float* x, double* stats, int64_t N, int64_t C, int64_t HW,
+                           void* workspace, size_t workspace_bytes, kbStream stream) {
+  const char* name = "kb_batchnorm_stats_f64";
+  if (int st = kb::bn_check(name, x, N, C, HW)) return st;
+  KB_REQUIRE(stats || C == 0, KB_ERR_INVALID_ARG, "%s: null stats", name);
+  if (C == 0) return KB_OK;
+  KB_REQUIRE(workspace && workspace_bytes >= kb_batchnorm_workspace_size(N, C, HW),
+             KB_ERR_WORKSPACE, "%s: workspace of %zu bytes needed", name,
+             kb_batchnorm_workspace_size(N, C, HW));
+  KB_REQUIRE((reinterpret_cast<uintptr_t>(workspace) & 15) == 0, KB_ERR_INVALID_ARG,
+             "%s: workspace must be 16-byte aligned", name);
+  const int S = kb::bn_splits(N, C);
+  const bool vec = HW % 4 == 0 && kb::aligned16(x);
+  double2* parts = static_cast<double2*>(workspace);
+  kb::BnShape sh{N, C, HW};
+  if (N > 0) {
+    kb::bn_stats_kernel<<<dim3((unsigned)C, (unsigned)S), kb::kThreads, 0, stream>>>(x, sh, S, vec, parts);
+    if (int st = kb::check_launch(name)) return st;
+    kb::bn_fold_kernel<<<(unsigned)kb::ceil_div(C, 128), 128, 0, stream>>>(parts, C, S, stats);
+  } else {
+    KB_CUDA(cudaMemsetAsync(stats, 0, sizeof(double) * 2 * C, stream));
+  }
+  return kb::check_launch(name);
+}
+
+int kb_batchnorm_apply_f32(const float* x, const float* gamma, const float* beta, float* y,
+                           const double* stats, int64_t N, int64_t C, int64_t HW,
+                           int64_t total_count, float eps, float momentum, float* running_mean,
+                           float* running_var, kbStream stream) {
+  const char* name = "kb_batchnorm_apply_f32";
+  if (int st = kb::bn_check(name, x, N, C, HW)) return st;
+  if (N * C * HW == 0) return KB_OK;
+  KB_REQUIRE(y && stats && total_count > 0, KB_ERR_INVALID_ARG, "%s: bad argument", name);
+  const bool vec = HW % 4 == 0 && kb::aligned16(x) && kb::aligned16(y);
+  kb::BnShape sh{N, C, HW};
+  kb::bn_apply_kernel<<<(unsigned)(N * C), kb::kThreads, 0, stream>>>(
+      x, gamma, beta, y, sh, nullptr, 0, stats, total_count, eps, momentum, running_mean,
+      running_var, vec);
+  return kb::check_launch(name);
+}
+
+}  // extern "C"

@@ -1,0 +1,79 @@
+// gemv.cu — y[M] = A[M, K] x[K], fp32, HBM-bound (0.5 FLOP/byte).
+//
+// One 512-thread CTA per row: the row (4 MB at K = 2^20) is streamed once
+// with 128-bit evict-first loads, 4 float4 of A and 4 of x in flight per
+// thread; x (4 MB) stays resident in the 126 MB L2 and is shared by every
+// CTA.  The row sum is a fixed shuffle tree, so y is deterministic (the
+// reference split rows into 32K chunks and combined them with fp32 atomics,
+// candidates/4_Matrix_vector_multiplication_/v1.py:16-33).  With 4 CTAs per
+// SM, 4096 rows are ~7 full waves over 148 SMs.
+#include "kb_common.cuh"
+
+namespace kb {
+namespace {
+
+constexpr int kThreads = 512;
+constexpr int kUnroll = 4;
+
+__global__ void __launch_bounds__(kThreads)
+gemv_vec4_kernel(const float* __restrict__ A, const float* __restrict__ x,
+                 float* __restrict__ y, int64_t K) {
+  __shared__ float red[32];
+  const int64_t row = blockIdx.x;
+  const float4* a4 = reinterpret_cast<const float4*>(A + row * K);
+  const float4* x4 = reinterpret_cast<const float4*>(x);
+  const int64_t nvec = K / 4;
+  float acc[kUnroll] = {0.f, 0.f, 0.f, 0.f};
+  int64_t i = threadIdx.x;
+  const int64_t step = (int64_t)kThreads * kUnroll;
+  for (; i + (kUnroll - 1) * kThreads < nvec; i += step) {
+    float4 a[kUnroll], b[kUnroll];
+#pragma unroll
+    for (int u = 0; u < kUnroll; ++u) {
+      a[u] = ld_stream(a4 + i + u * kThreads);
+      b[u] = __ldg(x4 + i + u * kThreads);
+    }
+#pragma unroll
+    for (int u = 0; u < kUnroll; ++u)
+      acc[u] = fmaf(a[u].x, b[u].x, fmaf(a[u].y, b[u].y, fmaf(a[u].z, b[u].z, fmaf(a[u].w, b[u].w, acc[u]))));
+  }
+  for (; i < nvec; i += kThreads) {
+    const float4 a = ld_stream(a4 + i), b = __ldg(x4 + i);
+    acc[0] = fmaf(a.x, b.x, fmaf(a.y, b.y, fmaf(a.z, b.z, fmaf(a.w, b.w, acc[0]))));
+  }
+  float s = (acc[0] + acc[1]) + (acc[2] + acc[3]);
+  for (int64_t j = nvec * 4 + threadIdx.x; j < K; j += kThreads) s = fmaf(A[row * K + j], x[j], s);
+  s = block_sum<kThreads>(s, red);
+  if (threadIdx.x == 0) y[row] = s;
+}
+
+__global__ void __launch_bounds__(kThreads)
+gemv_scalar_kernel(const float* __restrict__ A, const float* __restrict__ x,
+                   float* __restrict__ y, int64_t K) {
+  __shared__ float red[32];
+  const int64_t row = blockIdx.x;
+  float s = 0.f;
+  for (int64_t j = threadIdx.x; j < K; j += kThreads) s = fmaf(A[row * K + j], x[j], s);
+  s = block_sum<kThreads>(s, red);
+  if (threadIdx.x == 0) y[row] = s;
+}
+
+}  // namespace
+}  // namespace kb
+
+extern "C" {
+
+int kb_gemv_f32(const float* A, const float* x, float* y, int64_t M, int64_t K, kbStream stream) {
+  const char* name = "kb_gemv_f32";
+  KB_REQUIRE(M >= 0 && K >= 0, KB_ERR_INVALID_ARG, "%s: negative size", name);
+  if (M == 0) return KB_OK;
+  KB_REQUIRE(y && (K == 0 || (A && x)), KB_ERR_INVALID_ARG, "%s: null pointer", name);
+  KB_REQUIRE(M <= 0x7fffffff, KB_ERR_UNSUPPORTED, "%s: M too large", name);
+  if (K % 4 == 0 && kb::aligned16(A) && kb::aligned16(x))
+    kb::gemv_vec4_kernel<<<(unsigned)M, kb::kThreads, 0, stream>>>(A, x, y, K);
+  else
+    kb::gemv_scalar_kernel<<<(unsigned)M, kb::kThreads, 0, stream>>>(A, x, y, K);
+  return kb::check_launch(name);
+}
+
+}  // extern "C"

@@ -1,0 +1,258 @@
+// reduce.cu — global reductions to a scalar: MSE loss and Frobenius
+// normalisation, single-GPU and sharded (partial -> collective -> finish).
+//
+// Stage 1 is a persistent grid (SMs x 4 CTAs) that streams the input with
+// 128-bit loads and writes one fp64 partial per CTA into the caller's
+// workspace; stage 2 adds the partials in a fixed order.  No atomics: the
+// result is bit-reproducible run to run (the reference used one fp32 atomicAdd
+// per block, candidates/94_MSELoss/v1.py:27 and candidates/37_FrobeniusNorm_/
+// v1.py:33).  Per-thread sums run in fp32 over 16-element tiles and are then
+// promoted to fp64.
+//
+// Frobenius needs the global norm before any output can be written and the
+// input (1 GiB) does not fit on chip, so x is read twice.  The scale pass
+// walks the tensor from the end backwards so that its first tiles are the
+// ones the sum pass touched last, which are still resident in the 126 MB L2.
+#include "kb_common.cuh"
+
+namespace kb {
+namespace {
+
+constexpr int kThreads = 256;
+constexpr int kUnroll = 4;
+constexpr int kMaxPartials = 2048;
+
+int reduce_grid(int64_t nvec) {
+  const int64_t want = ceil_div(std::max<int64_t>(nvec, 1), (int64_t)kThreads * kUnroll);
+  return (int)std::max<int64_t>(1, std::min<int64_t>({want, (int64_t)sm_count() * 4, (int64_t)kMaxPartials}));
+}
+
+// sum over i of f(a[i], b[i]) -> partials[blockIdx.x]
+template <bool DIFF>
+__global__ void __launch_bounds__(kThreads)
+sq_partial_kernel(const float* __restrict__ a, const float* __restrict__ b, int64_t n,
+                  bool vec, double* __restrict__ partials) {
+  __shared__ double red[32];
+  double dacc = 0.0;
+  int64_t scalar_begin = 0;
+  if (vec) {
+    const int64_t nvec = n / 4;
+    const float4* a4 = reinterpret_cast<const float4*>(a);
+    const float4* b4 = reinterpret_cast<const float4*>(b);
+    const int64_t tile = (int64_t)kThreads * kUnroll;
+    const int64_t ntiles = nvec / tile;
+    for (int64_t t = blockIdx.x; t < ntiles; t += gridDim.x) {
+      const int64_t base = t * tile + threadIdx.x;
+      float4 va[kUnroll], vb[kUnroll];
+#pragma unroll
+      for (int u = 0; u < kUnroll; ++u) {
+        if constexpr (DIFF) {
+          va[u] = ld_stream(a4 + base + u * kThreads);
+          vb[u] = ld_stream(b4 + base + u * kThreads);
+        } else {
+          va[u] = __ldg(a4 + base + u * kThreads);  // keep in L2 for the scale pass
+        }
+      }
+      float s = 0.0f;
+#pragma unroll
+      for (int u = 0; u < kUnroll; ++u) {
+        float4 d = va[u];
+        if constexpr (DIFF) {
+          d.x -= vb[u].x; d.y -= vb[u].y; d.z -= vb[u].z; d.w -= vb[u].w;
+        }
+        s += (d.x * d.x + d.y * d.y) + (d.z * d.z + d.w * d.w);
+      }
+      dacc += (double)s;
+    }
+    for (int64_t i = ntiles * tile + (int64_t)blockIdx.x * kThreads + threadIdx.x; i < nvec;
+         i += (int64_t)gridDim.x * kThreads) {
+      float4 d = DIFF ? ld_stream(a4 + i) : __ldg(a4 + i);
+      if constexpr (DIFF) {
+        const float4 e = ld_stream(b4 + i);
+        d.x -= e.x; d.y -= e.y; d.z -= e.z; d.w -= e.w;
+      }
+      dacc += (double)((d.x * d.x + d.y * d.y) + (d.z * d.z + d.w * d.w));
+    }
+    scalar_begin = nvec * 4;
+  }
+  for (int64_t i = scalar_begin + (int64_t)blockIdx.x * kThreads + threadIdx.x; i < n;
+       i += (int64_t)gridDim.x * kThreads) {
+    float d = a[i];
+    if constexpr (DIFF) d -= b[i];
+    dacc += (double)(d * d);
+  }
+  const double tot = block_sum<kThreads>(dacc, red);
+  if (threadIdx.x == 0) partials[blockIdx.x] = tot;
+}
+
+// Fixed-order sum of `count` fp64 partials by one CTA (identical in every
+// CTA that calls it).
+__device__ __forceinline__ double sum_partials(const double* __restrict__ p, int count, double* red) {
+  double v = 0.0;
+  for (int i = threadIdx.x; i < count; i += kThreads) v += p[i];
+  return block_sum<kThreads>(v, red);
+}
+
+// mode 0: out_f = sum / denom (fp32); mode 1: out_d = sum (fp64)
+__global__ void __launch_bounds__(kThreads)
+finish_kernel(const double* __restrict__ partials, int count, double denom, float* out_f,
+              double* out_d) {
+  __shared__ double red[32];
+  const double s = sum_partials(partials, count, red);
+  if (threadIdx.x == 0) {
+    if (out_f) out_f[0] = (float)(s / denom);
+    if (out_d) out_d[0] = s;
+  }
+}
+
+__global__ void mse_finalize_kernel(const double* __restrict__ total, float* out, double denom) {
+  out[0] = (float)(total[0] / denom);
+}
+
+// y = x / sqrt(sumsq), walking tiles from the end of the tensor backwards.
+// sumsq comes either from `count` partials (single GPU) or from one fp64
+// total (sharded: count == 0).
+__global__ void __launch_bounds__(kThreads)
+scale_kernel(const float* __restrict__ x, float* __restrict__ y, int64_t n, bool vec,
+             const double* __restrict__ partials, int count) {
+  __shared__ double red[32];
+  const double ss = count > 0 ? sum_partials(partials, count, red) : partials[0];
+  const float norm = (float)sqrt(ss);
+  int64_t scalar_begin = 0;
+  if (vec) {
+    const int64_t nvec = n / 4;
+    const float4* x4 = reinterpret_cast<const float4*>(x);
+    float4* y4 = reinterpret_cast<float4*>(y);
+    const int64_t tile = (int64_t)kThreads * kUnroll;
+    const int64_t ntiles = nvec / tile;
+    for (int64_t i = ntiles * tile + (int64_t)blockIdx.x * kThreads + threadIdx.x; i < nvec;
+         i += (int64_t)gridDim.x * kThreads) {
+      const float4 v = __ldg(x4 + i);
+      st_stream(y4 + i, make_float4(v.x / norm, v.y / norm, v.z / norm, v.w / norm));
+    }
+    for (int64_t t = ntiles - 1 - blockIdx.x; t >= 0; t -= gridDim.x) {
+      const int64_t base = t * tile + threadIdx.x;
+      float4 v[kUnroll];
+#pragma unroll
+      for (int u = 0; u < kUnroll; ++u) v[u] = ld_stream(x4 + base + u * kThreads);
+#pragma unroll
+      for (int u = 0; u < kUnroll; ++u)
+        st_stream(y4 + base + u * kThreads,
+                  make_float4(v[u].x / norm, v[u].y / norm, v[u].z / norm, v[u].w / norm));
+    }
+    scalar_begin = nvec * 4;
+  }
+  for (int64_t i = scalar_begin + (int64_t)blockIdx.x * kThreads + threadIdx.x; i < n;
+       i += (int64_t)gridDim.x * kThreads)
+    y[i] = x[i] / norm;
+}
+
+int check_ws(const char* name, void* ws, size_t bytes, size_t need) {
+  KB_REQUIRE(ws != nullptr && bytes >= need, KB_ERR_WORKSPACE,
+             "%s: workspace of %zu bytes needed, %zu given", name, need, bytes);
+  KB_REQUIRE((reinterpret_cast<uintptr_t>(ws) & 7) == 0, KB_ERR_INVALID_ARG,
+             "%s: workspace must be 8-byte aligned", name);
+  return KB_OK;
+}
+
+// stage 1 for both ops; returns the number of partials written
+int launch_partials(const char* name, const float* a, const float* b, int64_t n, double* parts,
+                    cudaStream_t s, int* count) {
+  const bool vec = aligned16(a) && (!b || aligned16(b));
+  const int grid = reduce_grid(vec ? n / 4 : n);
+  if (b) sq_partial_kernel<true><<<grid, kThreads, 0, s>>>(a, b, n, vec, parts);
+  else sq_partial_kernel<false><<<grid, kThreads, 0, s>>>(a, nullptr, n, vec, parts);
+  *count = grid;
+  return check_launch(name);
+}
+
+}  // namespace
+}  // namespace kb
+
+extern "C" {
+
+size_t kb_mse_workspace_size(int64_t) { return kb::kMaxPartials * sizeof(double); }
+
+int kb_mse_f32(const float* a, const float* b, float* out, int64_t n, void* workspace,
+               size_t workspace_bytes, kbStream stream) {
+  const char* name = "kb_mse_f32";
+  KB_REQUIRE(n >= 0, KB_ERR_INVALID_ARG, "%s: negative n", name);
+  KB_REQUIRE(out && (n == 0 || (a && b)), KB_ERR_INVALID_ARG, "%s: null pointer", name);
+  if (int st = kb::check_ws(name, workspace, workspace_bytes, kb_mse_workspace_size(n))) return st;
+  double* parts = static_cast<double*>(workspace);
+  int count = 0;
+  if (n > 0) {
+    if (int st = kb::launch_partials(name, a, b, n, parts, stream, &count)) return st;
+  }
+  // n == 0: mean of nothing is NaN (0 / 0), as torch.mean of an empty tensor
+  kb::finish_kernel<<<1, kb::kThreads, 0, stream>>>(parts, count, (double)n, out, nullptr);
+  return kb::check_launch(name);
+}
+
+int kb_mse_partial_f64(const float* a, const float* b, double* partial, int64_t n,
+                       void* workspace, size_t workspace_bytes, kbStream stream) {
+  const char* name = "kb_mse_partial_f64";
+  KB_REQUIRE(n >= 0, KB_ERR_INVALID_ARG, "%s: negative n", name);
+  KB_REQUIRE(partial && (n == 0 || (a && b)), KB_ERR_INVALID_ARG, "%s: null pointer", name);
+  if (int st = kb::check_ws(name, workspace, workspace_bytes, kb_mse_workspace_size(n))) return st;
+  double* parts = static_cast<double*>(workspace);
+  int count = 0;
+  if (n > 0) {
+    if (int st = kb::launch_partials(name, a, b, n, parts, stream, &count)) return st;
+  }
+  kb::finish_kernel<<<1, kb::kThreads, 0, stream>>>(parts, count, 1.0, nullptr, partial);
+  return kb::check_launch(name);
+}
+
+int kb_mse_finalize_f32(const double* total, float* out, int64_t total_n, kbStream stream) {
+  KB_REQUIRE(total && out && total_n >= 0, KB_ERR_INVALID_ARG, "kb_mse_finalize_f32: bad argument");
+  kb::mse_finalize_kernel<<<1, 1, 0, stream>>>(total, out, (double)total_n);
+  return kb::check_launch("kb_mse_finalize_f32");
+}
+
+size_t kb_frobenius_workspace_size(int64_t) { return kb::kMaxPartials * sizeof(double); }
+
+int kb_frobenius_normalize_f32(const float* x, float* y, int64_t n, void* workspace,
+                               size_t workspace_bytes, kbStream stream) {
+  const char* name = "kb_frobenius_normalize_f32";
+  KB_REQUIRE(n >= 0, KB_ERR_INVALID_ARG, "%s: negative n", name);
+  if (n == 0) return KB_OK;
+  KB_REQUIRE(x && y, KB_ERR_INVALID_ARG, "%s: null pointer", name);
+  if (int st = kb::check_ws(name, workspace, workspace_bytes, kb_frobenius_workspace_size(n))) return st;
+  double* parts = static_cast<double*>(workspace);
+  int count = 0;
+  if (int st = kb::launch_partials(name, x, nullptr, n, parts, stream, &count)) return st;
+  const bool vec = kb::aligned16(x) && kb::aligned16(y);
+  const int grid = kb::reduce_grid(vec ? n / 4 : n);
+  kb::scale_kernel<<<grid, kb::kThreads, 0, stream>>>(x, y, n, vec, parts, count);
+  return kb::check_launch(name);
+}
+
+int kb_sumsq_partial_f64(const float* x, double* sumsq, int64_t n, void* workspace,
+                         size_t workspace_bytes, kbStream stream) {
+  const char* name = "kb_sumsq_partial_f64";
+  KB_REQUIRE(n >= 0, KB_ERR_INVALID_ARG, "%s: negative n", name);
+  KB_REQUIRE(sumsq && (n == 0 || x), KB_ERR_INVALID_ARG, "%s: null pointer", name);
+  if (int st = kb::check_ws(name, workspace, workspace_bytes, kb_frobenius_workspace_size(n))) return st;
+  double* parts = static_cast<double*>(workspace);
+  int count = 0;
+  if (n > 0) {
+    if (int st = kb::launch_partials(name, x, nullptr, n, parts, stream, &count)) return st;
+  }
+  kb::finish_kernel<<<1, kb::kThreads, 0, stream>>>(parts, count, 1.0, nullptr, sumsq);
+  return kb::check_launch(name);
+}
+
+int kb_scale_by_inv_norm_f32(const float* x, float* y, int64_t n, const double* total_sumsq,
+                             kbStream stream) {
+  const char* name = "kb_scale_by_inv_norm_f32";
+  KB_REQUIRE(n >= 0, KB_ERR_INVALID_ARG, "%s: negative n", name);
+  if (n == 0) return KB_OK;
+  KB_REQUIRE(x && y && total_sumsq, KB_ERR_INVALID_ARG, "%s: null pointer", name);
+  const bool vec = kb::aligned16(x) && kb::aligned16(y);
+  const int grid = kb::reduce_grid(vec ? n / 4 : n);
+  kb::scale_kernel<<<grid, kb::kThreads, 0, stream>>>(x, y, n, vec, total_sumsq, 0);
+  return kb::check_launch(name);
+}
+
+}  // extern "C"

@@ -1,0 +1,427 @@
+// rownorm.cu — single-read row kernels: LayerNorm, RMSNorm, softmax and
+// log-softmax over the last dimension, plus the channel-dim RMSNorm form.
+//
+// Design (B200): a row is read from HBM exactly once into registers
+// (VPT float4 per thread, 128-bit streaming loads), reduced on chip, and
+// written once.  Rows up to 16K floats live in one CTA; longer rows are split
+// across a thread-block cluster of CL CTAs whose partial statistics are
+// combined through distributed shared memory (DSMEM), so even a 128 KB
+// softmax row never round-trips through global memory.  Rows up to 1K floats
+// use one warp per row (shuffle-only reductions).  Shapes outside these
+// register-resident paths (cols % 4 != 0, unaligned views, > 128K columns)
+// take a generic multi-pass kernel.
+//
+// Two-pass statistics are done on the register copy: LayerNorm computes the
+// mean, then sum((x - mean)^2) — never E[x^2] - mean^2 (the cancellation-prone
+// form of candidates/40_LayerNorm/v1.py:44-46).
+#include <cooperative_groups.h>
+
+#include "kb_common.cuh"
+
+namespace cg = cooperative_groups;
+
+namespace kb {
+namespace {
+
+enum RowOp { kLayerNorm = 0, kRmsNorm = 1, kSoftmax = 2, kLogSoftmax = 3 };
+
+struct RowArgs {
+  const float* x;
+  const float* gamma;
+  const float* beta;
+  float* y;
+  int64_t rows;
+  int cols;
+  float eps;
+};
+
+// ---------------------------------------------------------------------------
+// reducers: warp-only, block, and block + cluster (DSMEM)
+// ---------------------------------------------------------------------------
+struct WarpReducer {
+  __device__ __forceinline__ float sum(float v, int) const { return warp_sum(v); }
+  __device__ __forceinline__ float max(float v, int) const { return warp_max(v); }
+};
+
+template <int NT, int CL>
+struct ClusterReducer {
+  float* red;    // >= 32 floats of shared memory
+  float* slots;  // >= 2 floats of shared memory, one per reduction stage
+  __device__ __forceinline__ float combine_sum(float part, int slot) const {
+    if constexpr (CL == 1) {
+      return part;
+    } else {
+      cg::cluster_group cluster = cg::this_cluster();
+      if (threadIdx.x == 0) slots[slot] = part;
+      cluster.sync();
+      float tot = 0.0f;
+#pragma unroll
+      for (int r = 0; r < CL; ++r) tot += *cluster.map_shared_rank(slots + slot, r);
+      return tot;
+    }
+  }
+  __device__ __forceinline__ float combine_max(float part, int slot) const {
+    if constexpr (CL == 1) {
+      return part;
+    } else {
+      cg::cluster_group cluster = cg::this_cluster();
+      if (threadIdx.x == 0) slots[slot] = part;
+      cluster.sync();
+      float m = -INFINITY;
+#pragma unroll
+      for (int r = 0; r < CL; ++r) m = fmaxf(m, *cluster.map_shared_rank(slots + slot, r));
+      return m;
+    }
+  }
+  __device__ __forceinline__ float sum(float v, int slot) const {
+    return combine_sum(block_sum<NT>(v, red), slot);
+  }
+  __device__ __forceinline__ float max(float v, int slot) const {
+    return combine_max(block_max<NT>(v, red), slot);
+  }
+};
+
+// ---------------------------------------------------------------------------
+// the per-row math on a register-resident segment
+//   v[k] holds float4 number (k * stride + lane) of this thread's segment;
+//   col4_base + k * stride + lane is its float4 index within the full row.
+// ---------------------------------------------------------------------------
+template <RowOp OP, int VPT, class R>
+__device__ __forceinline__ void row_math(float4 (&v)[VPT], const bool (&ok)[VPT],
+                                         const RowArgs& a, float4* yrow, int64_t col4_base,
+                                         int stride, int lane, const R& red) {
+  const float inv_cols = 1.0f / (float)a.cols;
+  if constexpr (OP == kLayerNorm) {
+    float s = 0.0f;
+#pragma unroll
+    for (int k = 0; k < VPT; ++k)
+      if (ok[k]) s += (v[k].x + v[k].y) + (v[k].z + v[k].w);
+    const float mean = red.sum(s, 0) * inv_cols;
+    float q = 0.0f;
+#pragma unroll
+    for (int k = 0; k < VPT; ++k)
+      if (ok[k]) {
+        float dx = v[k].x - mean, dy = v[k].y - mean, dz = v[k].z - mean, dw = v[k].w - mean;
+        q += (dx * dx + dy * dy) + (dz * dz + dw * dw);
+      }
+    const float var = red.sum(q, 1) * inv_cols;
+    const float rstd = 1.0f / sqrtf(var + a.eps);
+    const float4* g4 = reinterpret_cast<const float4*>(a.gamma);
+    const float4* b4 = reinterpret_cast<const float4*>(a.beta);
+#pragma unroll
+    for (int k = 0; k < VPT; ++k)
+      if (ok[k]) {
+        const int64_t c4 = col4_base + (int64_t)k * stride + lane;
+        float4 r;
+        r.x = (v[k].x - mean) * rstd;
+        r.y = (v[k].y - mean) * rstd;
+        r.z = (v[k].z - mean) * rstd;
+        r.w = (v[k].w - mean) * rstd;
+        if (g4) {
+          const float4 g = __ldg(g4 + c4);
+          r.x *= g.x; r.y *= g.y; r.z *= g.z; r.w *= g.w;
+        }
+        if (b4) {
+          const float4 b = __ldg(b4 + c4);
+          r.x += b.x; r.y += b.y; r.z += b.z; r.w += b.w;
+        }
+        st_stream(yrow + (int64_t)k * stride + lane, r);
+      }
+  } else if constexpr (OP == kRmsNorm) {
+    float q = 0.0f;
+#pragma unroll
+    for (int k = 0; k < VPT; ++k)
+      if (ok[k]) q += (v[k].x * v[k].x + v[k].y * v[k].y) + (v[k].z * v[k].z + v[k].w * v[k].w);
+    const float ms = red.sum(q, 0) * inv_cols;
+    const float inv = 1.0f / sqrtf(ms + a.eps);
+    const float4* g4 = reinterpret_cast<const float4*>(a.gamma);
+#pragma unroll
+    for (int k = 0; k < VPT; ++k)
+      if (ok[k]) {
+        const int64_t c4 = col4_base + (int64_t)k * stride + lane;
+        float4 r;
+        r.x = v[k].x * inv;
+        r.y = v[k].y * inv;
+        r.z = v[k].z * inv;
+        r.w = v[k].w * inv;
+        if (g4) {
+          const float4 g = __ldg(g4 + c4);
+          r.x *= g.x; r.y *= g.y; r.z *= g.z; r.w *= g.w;
+        }
+        st_stream(yrow + (int64_t)k * stride + lane, r);
+      }
+  } else {
+    float m = -INFINITY;
+#pragma unroll
+    for (int k = 0; k < VPT; ++k)
+      if (ok[k]) m = fmaxf(m, fmaxf(fmaxf(v[k].x, v[k].y), fmaxf(v[k].z, v[k].w)));
+    m = red.max(m, 0);
+    float s = 0.0f;
+    if constexpr (OP == kSoftmax) {
+      // keep exp(x - m) in registers: exp is evaluated once per element
+#pragma unroll
+      for (int k = 0; k < VPT; ++k)
+        if (ok[k]) {
+          v[k].x = expf(v[k].x - m);
+          v[k].y = expf(v[k].y - m);
+          v[k].z = expf(v[k].z - m);
+          v[k].w = expf(v[k].w - m);
+          s += (v[k].x + v[k].y) + (v[k].z + v[k].w);
+        }
+      const float inv = 1.0f / red.sum(s, 1);
+#pragma unroll
+      for (int k = 0; k < VPT; ++k)
+        if (ok[k]) {
+          float4 r = make_float4(v[k].x * inv, v[k].y * inv, v[k].z * inv, v[k].w * inv);
+          st_stream(yrow + (int64_t)k * stride + lane, r);
+        }
+    } else {
+#pragma unroll
+      for (int k = 0; k < VPT; ++k)
+        if (ok[k])
+          s += (expf(v[k].x - m) + expf(v[k].y - m)) + (expf(v[k].z - m) + expf(v[k].w - m));
+      const float lse = logf(red.sum(s, 1));
+#pragma unroll
+      for (int k = 0; k < VPT; ++k)
+        if (ok[k]) {
+          float4 r = make_float4((v[k].x - m) - lse, (v[k].y - m) - lse, (v[k].z - m) - lse,
+                                 (v[k].w - m) - lse);
+          st_stream(yrow + (int64_t)k * stride + lane, r);
+        }
+    }
+  }
+}
+
+// One CTA (or one CL-CTA cluster) per row; NT threads x VPT float4 each.
+template <RowOp OP, int NT, int VPT, int CL>
+__global__ void __launch_bounds__(NT) row_block_kernel(RowArgs a) {
+  __shared__ float red[32];
+  __shared__ float slots[2];
+  const int64_t row = blockIdx.x / CL;
+  int rank = 0;
+  if constexpr (CL > 1) rank = (int)cg::this_cluster().block_rank();
+  const int seg4 = a.cols / 4 / CL;  // float4s owned by this CTA
+  const int64_t col4_base = (int64_t)rank * seg4;
+  const float4* xs = reinterpret_cast<const float4*>(a.x + row * (int64_t)a.cols) + col4_base;
+  float4* ys = reinterpret_cast<float4*>(a.y + row * (int64_t)a.cols) + col4_base;
+  float4 v[VPT];
+  bool ok[VPT];
+#pragma unroll
+  for (int k = 0; k < VPT; ++k) {
+    const int i = k * NT + threadIdx.x;
+    ok[k] = i < seg4;
+    v[k] = ok[k] ? ld_stream(xs + i) : make_float4(0.f, 0.f, 0.f, 0.f);
+  }
+  ClusterReducer<NT, CL> r{red, slots};
+  row_math<OP, VPT>(v, ok, a, ys, col4_base, NT, threadIdx.x, r);
+  if constexpr (CL > 1) cg::this_cluster().sync();  // peers may still read `slots`
+}
+
+// One warp per row (rows of at most 32 * VPT * 4 floats); 4 warps per CTA.
+template <RowOp OP, int VPT>
+__global__ void __launch_bounds__(128) row_warp_kernel(RowArgs a) {
+  const int lane = threadIdx.x & 31;
+  const int64_t row = (int64_t)blockIdx.x * 4 + (threadIdx.x >> 5);
+  if (row >= a.rows) return;
+  const int n4 = a.cols / 4;
+  const float4* xs = reinterpret_cast<const float4*>(a.x + row * (int64_t)a.cols);
+  float4* ys = reinterpret_cast<float4*>(a.y + row * (int64_t)a.cols);
+  float4 v[VPT];
+  bool ok[VPT];
+#pragma unroll
+  for (int k = 0; k < VPT; ++k) {
+    const int i = k * 32 + lane;
+    ok[k] = i < n4;
+    v[k] = ok[k] ? ld_stream(xs + i) : make_float4(0.f, 0.f, 0.f, 0.f);
+  }
+  row_math<OP, VPT>(v, ok, a, ys, 0, 32, lane, WarpReducer{});
+}
+
+// Generic fallback: any cols, any alignment.  One 512-thread CTA per row,
+// the row is streamed from global memory once per pass (2-3 passes; later
+// passes mostly hit L2).
+template <RowOp OP>
+__global__ void __launch_bounds__(512) row_generic_kernel(RowArgs a) {
+  constexpr int NT = 512;
+  __shared__ float red[32];
+  const int64_t row = blockIdx.x;
+  const float* xr = a.x + row * (int64_t)a.cols;
+  float* yr = a.y + row * (int64_t)a.cols;
+  const int n = a.cols;
+  const float inv_cols = 1.0f / (float)n;
+  if constexpr (OP == kLayerNorm) {
+    float s = 0.f;
+    for (int i = threadIdx.x; i < n; i += NT) s += xr[i];
+    const float mean = block_sum<NT>(s, red) * inv_cols;
+    float q = 0.f;
+    for (int i = threadIdx.x; i < n; i += NT) {
+      float d = xr[i] - mean;
+      q += d * d;
+    }
+    const float rstd = 1.0f / sqrtf(block_sum<NT>(q, red) * inv_cols + a.eps);
+    for (int i = threadIdx.x; i < n; i += NT) {
+      float r = (xr[i] - mean) * rstd;
+      if (a.gamma) r *= a.gamma[i];
+      if (a.beta) r += a.beta[i];
+      yr[i] = r;
+    }
+  } else if constexpr (OP == kRmsNorm) {
+    float q = 0.f;
+    for (int i = threadIdx.x; i < n; i += NT) q += xr[i] * xr[i];
+    const float inv = 1.0f / sqrtf(block_sum<NT>(q, red) * inv_cols + a.eps);
+    for (int i = threadIdx.x; i < n; i += NT) {
+      float r = xr[i] * inv;
+      if (a.gamma) r *= a.gamma[i];
+      yr[i] = r;
+    }
+  } else {
+    float m = -INFINITY;
+    for (int i = threadIdx.x; i < n; i += NT) m = fmaxf(m, xr[i]);
+    m = block_max<NT>(m, red);
+    float s = 0.f;
+    for (int i = threadIdx.x; i < n; i += NT) s += expf(xr[i] - m);
+    s = block_sum<NT>(s, red);
+    if constexpr (OP == kSoftmax) {
+      const float inv = 1.0f / s;
+      for (int i = threadIdx.x; i < n; i += NT) yr[i] = expf(xr[i] - m) * inv;
+    } else {
+      const float lse = logf(s);
+      for (int i = threadIdx.x; i < n; i += NT) yr[i] = (xr[i] - m) - lse;
+    }
+  }
+}
+
+template <RowOp OP, int NT, int VPT, int CL>
+cudaError_t launch_block(const RowArgs& a, cudaStream_t s) {
+  auto kern = row_block_kernel<OP, NT, VPT, CL>;
+  if constexpr (CL == 1) {
+    kern<<<(unsigned)a.rows, NT, 0, s>>>(a);
+    return cudaGetLastError();
+  } else {
+    cudaLaunchConfig_t cfg = {};
+    cfg.gridDim = dim3((unsigned)(a.rows * CL));
+    cfg.blockDim = dim3(NT);
+    cfg.dynamicSmemBytes = 0;
+    cfg.stream = s;
+    cudaLaunchAttribute attr[1];
+    attr[0].id = cudaLaunchAttributeClusterDimension;
+    attr[0].val.clusterDim.x = CL;
+    attr[0].val.clusterDim.y = 1;
+    attr[0].val.clusterDim.z = 1;
+    cfg.attrs = attr;
+    cfg.numAttrs = 1;
+    return cudaLaunchKernelEx(&cfg, kern, a);
+  }
+}
+
+template <RowOp OP>
+int launch_rows(const char* name, const RowArgs& a, cudaStream_t s) {
+  KB_REQUIRE(a.rows >= 0 && a.cols >= 0, KB_ERR_INVALID_ARG, "%s: negative size", name);
+  if (a.rows == 0 || a.cols == 0) return KB_OK;
+  KB_REQUIRE(a.x && a.y, KB_ERR_INVALID_ARG, "%s: null pointer", name);
+  KB_REQUIRE(a.rows <= 0x7fffffffLL / 8, KB_ERR_UNSUPPORTED, "%s: too many rows", name);
+  const bool vec = (a.cols % 4 == 0) && aligned16(a.x) && aligned16(a.y) &&
+                   (!a.gamma || aligned16(a.gamma)) && (!a.beta || aligned16(a.beta));
+  const int c = a.cols;
+  cudaError_t e = cudaSuccess;
+  if (!vec || c > 131072) {
+    row_generic_kernel<OP><<<(unsigned)a.rows, 512, 0, s>>>(a);
+    e = cudaGetLastError();
+  } else if (c <= 1024) {
+    const unsigned grid = (unsigned)ceil_div(a.rows, 4);
+    if (c <= 128) row_warp_kernel<OP, 1><<<grid, 128, 0, s>>>(a);
+    else if (c <= 256) row_warp_kernel<OP, 2><<<grid, 128, 0, s>>>(a);
+    else if (c <= 512) row_warp_kernel<OP, 4><<<grid, 128, 0, s>>>(a);
+    else row_warp_kernel<OP, 8><<<grid, 128, 0, s>>>(a);
+    e = cudaGetLastError();
+  } else if (c <= 2048) {
+    e = launch_block<OP, 128, 4, 1>(a, s);
+  } else if (c <= 4096) {
+    e = launch_block<OP, 256, 4, 1>(a, s);
+  } else if (c <= 8192) {
+    e = launch_block<OP, 256, 8, 1>(a, s);
+  } else if (c <= 16384) {
+    e = launch_block<OP, 512, 8, 1>(a, s);
+  } else if (c <= 32768 && c % 8 == 0) {
+    e = launch_block<OP, 512, 8, 2>(a, s);
+  } else if (c <= 65536 && c % 16 == 0) {
+    e = launch_block<OP, 512, 8, 4>(a, s);
+  } else if (c % 32 == 0) {
+    e = launch_block<OP, 512, 8, 8>(a, s);
+  } else {
+    row_generic_kernel<OP><<<(unsigned)a.rows, 512, 0, s>>>(a);
+    e = cudaGetLastError();
+  }
+  if (e != cudaSuccess) return set_error(KB_ERR_CUDA, "%s launch: %s", name, cudaGetErrorString(e));
+  return KB_OK;
+}
+
+// ---------------------------------------------------------------------------
+// RMSNorm over dim 1 of [outer, F, inner] (inner > 1): thread per (outer,
+// inner) position, coalesced across inner; features walked twice (the second
+// walk re-reads the CTA's 64-feature x 256-position window from L2).
+// Follows the fixed addressing of candidates/36_RMSNorm_/v3.py:17-19.
+// ---------------------------------------------------------------------------
+__global__ void __launch_bounds__(256)
+rms_channel_kernel(const float* __restrict__ x, const float* __restrict__ gamma,
+                   float* __restrict__ y, int64_t outer, int64_t F, int64_t inner, float eps) {
+  const int64_t p = (int64_t)blockIdx.x * 256 + threadIdx.x;
+  if (p >= outer * inner) return;
+  const int64_t o = p / inner, i = p - o * inner;
+  const float* xp = x + o * F * inner + i;
+  float* yp = y + o * F * inner + i;
+  float q = 0.f;
+  for (int64_t f = 0; f < F; ++f) {
+    const float v = xp[f * inner];
+    q += v * v;
+  }
+  const float inv = 1.0f / sqrtf(q / (float)F + eps);
+  for (int64_t f = 0; f < F; ++f) {
+    float r = xp[f * inner] * inv;
+    if (gamma) r *= gamma[f];
+    yp[f * inner] = r;
+  }
+}
+
+}  // namespace
+}  // namespace kb
+
+extern "C" {
+
+int kb_layernorm_f32(const float* x, const float* gamma, const float* beta, float* y,
+                     int64_t rows, int64_t cols, float eps, kbStream stream) {
+  KB_REQUIRE(cols <= 0x7fffffff, KB_ERR_UNSUPPORTED, "kb_layernorm_f32: cols too large");
+  kb::RowArgs a{x, gamma, beta, y, rows, (int)cols, eps};
+  return kb::launch_rows<kb::kLayerNorm>("kb_layernorm_f32", a, stream);
+}
+
+int kb_rmsnorm_f32(const float* x, const float* gamma, float* y, int64_t outer,
+                   int64_t features, int64_t inner, float eps, kbStream stream) {
+  KB_REQUIRE(outer >= 0 && features >= 0 && inner >= 1, KB_ERR_INVALID_ARG,
+             "kb_rmsnorm_f32: bad shape");
+  if (outer == 0 || features == 0) return KB_OK;
+  if (inner == 1) {
+    KB_REQUIRE(features <= 0x7fffffff, KB_ERR_UNSUPPORTED, "kb_rmsnorm_f32: features too large");
+    kb::RowArgs a{x, gamma, nullptr, y, outer, (int)features, eps};
+    return kb::launch_rows<kb::kRmsNorm>("kb_rmsnorm_f32", a, stream);
+  }
+  KB_REQUIRE(x && y, KB_ERR_INVALID_ARG, "kb_rmsnorm_f32: null pointer");
+  const int64_t pos = outer * inner;
+  kb::rms_channel_kernel<<<(unsigned)kb::ceil_div(pos, 256), 256, 0, stream>>>(
+      x, gamma, y, outer, features, inner, eps);
+  return kb::check_launch("kb_rmsnorm_f32");
+}
+
+int kb_softmax_f32(const float* x, float* y, int64_t rows, int64_t cols, kbStream stream) {
+  KB_REQUIRE(cols <= 0x7fffffff, KB_ERR_UNSUPPORTED, "kb_softmax_f32: cols too large");
+  kb::RowArgs a{x, nullptr, nullptr, y, rows, (int)cols, 0.f};
+  return kb::launch_rows<kb::kSoftmax>("kb_softmax_f32", a, stream);
+}
+
+int kb_logsoftmax_f32(const float* x, float* y, int64_t rows, int64_t cols, kbStream stream) {
+  KB_REQUIRE(cols <= 0x7fffffff, KB_ERR_UNSUPPORTED, "kb_logsoftmax_f32: cols too large");
+  kb::RowArgs a{x, nullptr, nullptr, y, rows, (int)cols, 0.f};
+  return kb::launch_rows<kb::kLogSoftmax>("kb_logsoftmax_f32", a, stream);
+}
+
+}  // extern "C"

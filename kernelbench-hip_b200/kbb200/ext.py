@@ -1,0 +1,137 @@
+"""The compiled-entry surface the candidates call (`EXT.<ENTRY>(...)`).
+
+Each function keeps the name and argument meaning of the reference
+candidate's C++ entry (outputs preallocated by the caller, asynchronous launch
+on the current stream, no return value) and forwards to the C ABI through
+kbb200.ops.  Where the reference entry took scratch tensors that only served
+its atomics (mean/var for LayerNorm, sum/sumsq for BatchNorm), the slot now
+carries the affine parameters instead; the entry docstrings say so.
+"""
+from __future__ import annotations
+
+import torch
+
+from . import ops
+
+
+def mingpt_gelu_entry(x: torch.Tensor, y: torch.Tensor) -> None:
+    """candidates/88_MinGPTNewGelu/v1.py:21 — tanh-approx GELU."""
+    ops.gelu_tanh(x, out=y)
+
+
+def gelu_entry(x: torch.Tensor, y: torch.Tensor) -> None:
+    """candidates/26_GELU_/v1.py:18 — exact (erf) GELU."""
+    ops.gelu_erf(x, out=y)
+
+
+def swish_entry(x: torch.Tensor, y: torch.Tensor) -> None:
+    """candidates/25_Swish/v1.py:18."""
+    ops.swish(x, out=y)
+
+
+def relu_entry(x: torch.Tensor, y: torch.Tensor) -> None:
+    """candidates/19_ReLU/v1.py:15."""
+    ops.relu(x, out=y)
+
+
+def softmax_entry(x: torch.Tensor, y: torch.Tensor) -> None:
+    """candidates/23_Softmax/v1.py:47 — softmax over the last dim."""
+    ops.softmax(x, out=y)
+
+
+def logsoftmax_entry(x: torch.Tensor, y: torch.Tensor) -> None:
+    """candidates/24_LogSoftmax/v1.py:46 — log-softmax over the last dim."""
+    ops.log_softmax(x, out=y)
+
+
+def layernorm_entry(x, y, weight, bias, eps: float) -> None:
+    """candidates/40_LayerNorm/v1.py:62 — (x, y, mean, var, eps) there; the two
+    scratch slots carry weight and bias here (None = identity affine).  The
+    normalized size is weight.numel(), else the last dim."""
+    ops.layer_norm(x, weight, bias, eps, out=y)
+
+
+def rmsnorm_entry(x, y, weight, eps: float, rows: int, F: int, inner: int) -> None:
+    """candidates/36_RMSNorm_/v3.py:42 — (x, y, rms, eps, rows, F, inner) there;
+    x is [rows / inner, F, inner] normalised over F.  The scratch slot carries
+    the optional per-feature weight."""
+    fn = "rmsnorm_entry"
+    if inner <= 0 or rows % inner or x.numel() != rows * F:
+        raise RuntimeError(f"{fn}: rows={rows}, F={F}, inner={inner} do not describe x{tuple(x.shape)}")
+    ops._check_f32(fn, x, y, weight)
+    from ._lib import LIB, check
+    check("kb_rmsnorm_f32", LIB.kb_rmsnorm_f32(x.data_ptr(), ops._ptr(weight), y.data_ptr(),
+                                               rows // inner, F, inner, float(eps), ops._stream(x)))
+
+
+def colreduce_entry(x, out, mean_mode: int) -> None:
+    """candidates/47_Sum_reduction_over_a_dimension/v1.py:28 — out[b, j] =
+    sum (or mean when mean_mode) over dim 1 of x[B, I, J]."""
+    B, I, J = x.shape
+    if mean_mode:
+        ops.mean_dim(x, 1, out=out)
+    else:
+        ops.sum_dim(x, 1, out=out)
+
+
+def colreduce_mean_entry(x, out, mean_mode: int) -> None:
+    """candidates/48_Mean_reduction_over_a_dimension/v1.py:25."""
+    colreduce_entry(x, out, mean_mode)
+
+
+def argmax_entry(x, out) -> None:
+    """candidates/51_Argmax_over_a_dimension/v1.py:27 — int64 indices over dim 1."""
+    ops.argmax_dim(x, 1, out=out)
+
+
+def mse_entry(p, t, out) -> None:
+    """candidates/94_MSELoss/v1.py:35 — out (0-d) = mean((p - t)^2)."""
+    ops.mse_loss(p, t, out=out)
+
+
+def frobenius_entry(x, y, scratch=None) -> None:
+    """candidates/37_FrobeniusNorm_/v1.py:48 — y = x / ||x||_F.  `scratch`, when
+    given, must hold kb_frobenius_workspace_size bytes (any dtype)."""
+    from ._lib import LIB, check
+    fn = "kb_frobenius_normalize_f32"
+    ops._check_f32(fn, x, y)
+    n = x.numel()
+    need = LIB.kb_frobenius_workspace_size(n)
+    if scratch is None or scratch.numel() * scratch.element_size() < need:
+        scratch = ops._workspace(x, need)
+    check(fn, LIB.kb_frobenius_normalize_f32(x.data_ptr(), y.data_ptr(), n, scratch.data_ptr(),
+                                             scratch.numel() * scratch.element_size(), ops._stream(x)))
+
+
+def maxpool_entry(x, y, K: int, pad: int, stride: int | None = None, dilation: int = 1) -> None:
+    """candidates/42_Max_Pooling_2D/v1.py:37 — (x, y, K, pad) there, which
+    silently assumed stride 1 and dilation 1; both are explicit here."""
+    ops.max_pool2d(x, K, stride if stride is not None else 1, pad, dilation, out=y)
+
+
+def bn_entry(x, y, weight, bias, eps: float, momentum: float = 0.1, running_mean=None,
+             running_var=None) -> None:
+    """candidates/33_BatchNorm/v1.py:53 — (x, y, sum, sumsq, eps) there; the
+    scratch slots carry the affine parameters here (None = identity)."""
+    ops.batch_norm_train(x, weight, bias, eps, momentum, running_mean, running_var, out=y)
+
+
+def sgemm_entry(A, B, C, trans_a: int, batches: int) -> None:
+    """candidates/1_Square_matrix_multiplication_/v1.py:83 (also 3_Batched,
+    13_Symmetric, 16_TransposedA): C = op(A) @ B, batched when batches > 1."""
+    if batches > 1:
+        ops.bmm(A, B, out=C)
+    else:
+        ops.matmul(A, B, trans_a=bool(trans_a), out=C)
+
+
+def splitk_gemm_entry(A, B, C, split: int = 0) -> None:
+    """candidates/6_Matmul_with_large_K_dimension_/v1.py:67 — the split count
+    is chosen by the library (one K slice per SM); `split` is accepted for
+    signature compatibility."""
+    ops.matmul_splitk(A, B, out=C)
+
+
+def gemv_entry(A, B, C) -> None:
+    """candidates/4_Matrix_vector_multiplication_/v1.py:36 — C = A @ B, B [K] or [K, 1]."""
+    ops.gemv(A, B, out=C)

@@ -1,0 +1,294 @@
+"""GPU parity: the CUDA kernels (called through the C ABI via kbb200.ops)
+against the golden fixtures, the numpy oracle, and — at the benchmark
+shapes — torch's own fp32 eager ops on the same device.
+
+Tolerances (tests/opmap.py): atol = rtol = 1e-5 elementwise / norm ops,
+1e-3 reductions and contractions, bit-exact argmax and max-pool.
+"""
+from __future__ import annotations
+
+import math
+
+import numpy as np
+import pytest
+import torch
+import torch.nn.functional as F
+
+from oracle import ops as O
+from oracle import problems
+from tests.opmap import EXACT, ORACLE, assert_close, gpu_call, load_golden
+
+pytestmark = pytest.mark.gpu
+
+GEMMS = {"1_Square_matrix_multiplication_", "3_Batched_matrix_multiplication",
+         "6_Matmul_with_large_K_dimension_"}
+
+
+def _dev(arrs, device):
+    return [torch.from_numpy(np.ascontiguousarray(a)).to(device) for a in arrs]
+
+
+@pytest.mark.parametrize("name", problems.SUBSET)
+def test_golden(name, cuda_device):
+    ins, out, _ = load_golden(name)
+    got = gpu_call(name)(*_dev(ins, cuda_device))
+    torch.cuda.synchronize()
+    _, tol = ORACLE[name]
+    assert_close(got.cpu().numpy(), out, tol, f"{name} vs golden")
+
+
+@pytest.mark.parametrize("name", problems.SUBSET)
+@pytest.mark.parametrize("seed", [0, 1])
+def test_small_vs_oracle(name, seed, cuda_device):
+    Model, get_inputs, get_init_inputs, _ = problems.load_problem(name, "small")
+    torch.manual_seed(seed)
+    inputs = get_inputs()
+    fn, tol = ORACLE[name]
+    want = fn(*[t.numpy() for t in inputs])
+    got = gpu_call(name)(*[t.to(cuda_device) for t in inputs]).cpu().numpy()
+    assert_close(got, want, tol, f"{name} seed {seed}")
+
+
+# ------------------------------------------------------------ kernel-path coverage
+@pytest.mark.parametrize("n", [1, 3, 4, 1023, 4096, 1 << 20, (1 << 20) + 5, 3 * 1024 * 1024 + 7])
+@pytest.mark.parametrize("op", ["gelu_tanh", "gelu_erf", "swish", "relu"])
+def test_elementwise_sizes_and_tails(op, n, cuda_device):
+    from kbb200 import ops as K
+
+    g = torch.Generator().manual_seed(n)
+    x = torch.randn(n, generator=g) * 4
+    ref = getattr(O, op)(x.numpy())
+    got = getattr(K, op)(x.to(cuda_device)).cpu().numpy()
+    assert_close(got, ref, EXACT if op == "relu" else 1e-5, f"{op} n={n}")
+
+
+@pytest.mark.parametrize("op", ["gelu_tanh", "relu", "swish"])
+def test_elementwise_unaligned_view(op, cuda_device):
+    from kbb200 import ops as K
+
+    base = torch.randn(10007, device=cuda_device)
+    x = base[1:]                       # 4-byte offset: scalar path
+    y = torch.empty(10006, device=cuda_device)
+    getattr(K, op)(x, out=y)
+    assert_close(y.cpu().numpy(), getattr(O, op)(x.cpu().numpy()), EXACT if op == "relu" else 1e-5)
+
+
+def test_relu_special_values(cuda_device):
+    from kbb200 import ops as K
+
+    x = torch.tensor([-0.0, 0.0, float("nan"), -1.0, 2.0, float("-inf"), float("inf")])
+    got = K.relu(x.to(cuda_device)).cpu()
+    ref = torch.relu(x)
+    assert torch.equal(torch.signbit(got), torch.signbit(ref))
+    assert_close(got.numpy(), ref.numpy(), EXACT)
+
+
+ROW_COLS = [4, 100, 128, 256, 512, 1000, 1024, 1536, 2048, 4096, 6000, 8192, 12288, 16384,
+            20000, 32768, 40000, 65536, 100000, 131072, 131076, 200000, 1001, 4097]
+
+
+@pytest.mark.parametrize("cols", ROW_COLS)
+@pytest.mark.parametrize("op", ["layer_norm", "rms_norm", "softmax", "log_softmax"])
+def test_row_ops_all_paths(op, cols, cuda_device):
+    from kbb200 import ops as K
+
+    rows = 3 if cols > 50000 else 7
+    g = torch.Generator().manual_seed(cols)
+    x = torch.randn(rows, cols, generator=g) * 2 + 0.5
+    w = 1 + 0.1 * torch.randn(cols, generator=g)
+    b = 0.1 * torch.randn(cols, generator=g)
+    xd, wd, bd = x.to(cuda_device), w.to(cuda_device), b.to(cuda_device)
+    if op == "layer_norm":
+        got, want = K.layer_norm(xd, wd, bd), O.layer_norm(x.numpy(), w.numpy(), b.numpy())
+    elif op == "rms_norm":
+        got, want = K.rms_norm(xd, wd), O.rms_norm(x.numpy(), w.numpy())
+    elif op == "softmax":
+        got, want = K.softmax(xd), O.softmax(x.numpy())
+    else:
+        got, want = K.log_softmax(xd), O.log_softmax(x.numpy())
+    assert_close(got.cpu().numpy(), want, 1e-5, f"{op} cols={cols}")
+
+
+@pytest.mark.parametrize("op", ["layer_norm", "softmax"])
+def test_row_ops_unaligned_and_no_affine(op, cuda_device):
+    from kbb200 import ops as K
+
+    base = torch.randn(5 * 2048 + 1, device=cuda_device)
+    x = base[1:].view(5, 2048)          # misaligned rows -> generic kernel
+    if op == "layer_norm":
+        got, want = K.layer_norm(x), O.layer_norm(x.cpu().numpy())
+    else:
+        got, want = K.softmax(x), O.softmax(x.cpu().numpy())
+    assert_close(got.cpu().numpy(), want, 1e-5, op)
+
+
+def test_rmsnorm_channel_form(cuda_device):
+    from kbb200 import ops as K
+
+    x = torch.randn(4, 64, 17, 19)
+    got = K.rms_norm(x.to(cuda_device), None, 1e-5, dim=1).cpu().numpy()
+    ref = (x / torch.sqrt(torch.mean(x ** 2, dim=1, keepdim=True) + 1e-5)).numpy()
+    assert_close(got, ref, 1e-5, "rms dim=1")
+
+
+def test_softmax_extremes(cuda_device):
+    from kbb200 import ops as K
+
+    x = torch.tensor([[0.0, float("-inf"), 1.0, 1.0] * 1024, [1e4, -1e4, 0.0, 3.0] * 1024])
+    got = K.softmax(x.to(cuda_device)).cpu()
+    assert_close(got.numpy(), torch.softmax(x, -1).numpy(), 1e-5)
+    got = K.log_softmax(x.to(cuda_device)).cpu()
+    assert_close(got.numpy(), torch.log_softmax(x, -1).numpy(), 1e-5)
+
+
+@pytest.mark.parametrize("shape", [(2, 5, 4), (3, 1000, 129), (1, 7, 1), (2, 4097, 260), (5, 3, 4096)])
+@pytest.mark.parametrize("op", ["sum_dim", "mean_dim", "argmax_dim"])
+def test_colreduce_shapes(op, shape, cuda_device):
+    from kbb200 import ops as K
+
+    g = torch.Generator().manual_seed(sum(shape))
+    x = torch.rand(shape, generator=g) * 2 - 1
+    got = getattr(K, op)(x.to(cuda_device), 1).cpu().numpy()
+    want = getattr(O, op)(x.numpy(), 1)
+    assert_close(got, want, EXACT if op == "argmax_dim" else 1e-3, f"{op} {shape}")
+
+
+def test_argmax_ties_nan_and_quantised_values(cuda_device):
+    from kbb200 import ops as K
+
+    g = torch.Generator().manual_seed(5)
+    x = torch.randint(0, 4, (3, 1030, 260), generator=g).float()  # many ties
+    x[0, 500, 7] = float("nan")
+    x[1, 3, 11] = float("nan")
+    x[1, 900, 11] = float("nan")
+    x[2, :, 5] = float("-inf")
+    got = K.argmax_dim(x.to(cuda_device), 1).cpu()
+    assert torch.equal(got, torch.argmax(x, 1))
+    assert_close(got.numpy(), O.argmax_dim(x.numpy(), 1), EXACT)
+
+
+@pytest.mark.parametrize("n", [0, 1, 5, 4096, 1 << 20, (1 << 22) + 3])
+def test_mse_sizes(n, cuda_device):
+    from kbb200 import ops as K
+
+    g = torch.Generator().manual_seed(n + 1)
+    a, b = torch.randn(n, generator=g), torch.randn(n, generator=g)
+    got = K.mse_loss(a.to(cuda_device), b.to(cuda_device)).cpu().numpy()
+    assert_close(got, O.mse_loss(a.numpy(), b.numpy()), 1e-3, f"mse n={n}")
+
+
+def test_mse_is_deterministic(cuda_device):
+    from kbb200 import ops as K
+
+    a = torch.randn(1 << 24, device=cuda_device)
+    b = torch.randn(1 << 24, device=cuda_device)
+    r = [K.mse_loss(a, b).item() for _ in range(3)]
+    assert r[0] == r[1] == r[2]
+
+
+@pytest.mark.parametrize("shape", [(1,), (7, 13), (3, 64, 129), (1 << 20,), (5, 1 << 18)])
+def test_frobenius_shapes(shape, cuda_device):
+    from kbb200 import ops as K
+
+    x = torch.randn(shape)
+    got = K.frobenius_normalize(x.to(cuda_device)).cpu().numpy()
+    assert_close(got, O.frobenius_normalize(x.numpy()), 1e-5, f"fro {shape}")
+
+
+@pytest.mark.parametrize("cfg", [(3, 2, 1, 1), (2, 2, 0, 1), (3, 1, 1, 1), (4, 3, 2, 1), (3, 2, 1, 2),
+                                 (2, 1, 0, 3)])
+@pytest.mark.parametrize("hw", [(32, 128), (31, 45), (128, 256), (7, 128)])
+def test_maxpool_configs(cfg, hw, cuda_device):
+    from kbb200 import ops as K
+
+    k, s, p, d = cfg
+    H, W = hw
+    if (H + 2 * p - d * (k - 1) - 1) < 0 or (W + 2 * p - d * (k - 1) - 1) < 0:
+        pytest.skip("window larger than input")
+    x = torch.randn(2, 3, H, W)
+    got = K.max_pool2d(x.to(cuda_device), k, s, p, d).cpu().numpy()
+    ref = F.max_pool2d(x, k, s, p, d).numpy()
+    assert_close(got, ref, EXACT, f"pool {cfg} {hw}")
+
+
+def test_maxpool_nan(cuda_device):
+    from kbb200 import ops as K
+
+    x = torch.randn(1, 2, 16, 128)
+    x[0, 0, 5, 9] = float("nan")
+    x[0, 1, 0, 0] = float("nan")
+    got = K.max_pool2d(x.to(cuda_device), 3, 2, 1).cpu().numpy()
+    assert_close(got, F.max_pool2d(x, 3, 2, 1).numpy(), EXACT)
+
+
+@pytest.mark.parametrize("shape", [(2, 3, 4, 4), (3, 128, 6, 10), (5, 7, 9, 11), (64, 8, 32, 32)])
+def test_batchnorm_shapes_and_running_stats(shape, cuda_device):
+    from kbb200 import ops as K
+
+    g = torch.Generator().manual_seed(7)
+    x = torch.randn(shape, generator=g) * 1.5 + 0.3
+    C = shape[1]
+    w = 1 + 0.02 * torch.randn(C, generator=g)
+    b = 0.02 * torch.randn(C, generator=g)
+    rm = torch.zeros(C, device=cuda_device)
+    rv = torch.ones(C, device=cuda_device)
+    got = K.batch_norm_train(x.to(cuda_device), w.to(cuda_device), b.to(cuda_device), 1e-5, 0.1,
+                             rm, rv).cpu().numpy()
+    assert_close(got, O.batch_norm_train(x.numpy(), w.numpy(), b.numpy()), 1e-5, f"bn {shape}")
+    erm, erv = O.batch_norm_running_update(x.numpy(), np.zeros(C), np.ones(C))
+    np.testing.assert_allclose(rm.cpu().numpy(), erm, rtol=1e-5, atol=1e-6)
+    np.testing.assert_allclose(rv.cpu().numpy(), erv, rtol=1e-5, atol=1e-6)
+
+
+@pytest.mark.parametrize("mk", [(1, 1), (3, 7), (17, 1031), (64, 4096), (5, 100003)])
+def test_gemv_shapes(mk, cuda_device):
+    from kbb200 import ops as K
+
+    M, Kd = mk
+    A, x = torch.randn(M, Kd), torch.randn(Kd)
+    got = K.gemv(A.to(cuda_device), x.to(cuda_device)).cpu().numpy()
+    assert_close(got, O.gemv(A.numpy(), x.numpy()), 1e-3, f"gemv {mk}")
+
+
+# ------------------------------------------------------------ benchmark shapes vs torch eager
+FULL = [n for n in problems.SUBSET if n not in GEMMS]
+
+
+@pytest.mark.parametrize("name", FULL)
+def test_full_size_vs_torch_eager(name, cuda_device):
+    """Benchmark-shape parity against the reference arm (torch eager fp32) on
+    the same device and the same seeded inputs."""
+    from kbb200.workloads import WORKLOADS, make_inputs
+
+    w = next(w for w in WORKLOADS.values() if w.problem == name)
+    Model, _, get_init_inputs, _ = problems.load_problem(name)
+    inputs = make_inputs(w, cuda_device, seed=0)      # seeded on the device
+    ref_model = Model(*get_init_inputs()).to(cuda_device)
+    with torch.no_grad():
+        want = ref_model(*inputs)
+    got = gpu_call(name)(*inputs)
+    torch.cuda.synchronize()
+    _, tol = ORACLE[name]
+    if tol == EXACT:
+        assert torch.equal(got, want.to(got.dtype)), name
+    else:
+        ok = torch.isclose(got, want, atol=tol, rtol=tol)
+        bad = (~ok).sum().item()
+        assert bad == 0, f"{name}: {bad} elements outside atol=rtol={tol}; max diff " \
+                         f"{(got - want).abs().max().item():.3e}"
+    del inputs, want, got
+    torch.cuda.empty_cache()
+
+
+def test_full_size_row_sums(cuda_device):
+    """Size-independent property at the softmax benchmark shape: every row of
+    softmax sums to 1 and exp(log_softmax) equals softmax."""
+    from kbb200 import ops as K
+
+    g = torch.Generator(device=cuda_device).manual_seed(0)
+    x = torch.randn(8192, 32768, device=cuda_device, generator=g) * 2
+    s = K.softmax(x)
+    torch.testing.assert_close(s.double().sum(-1), torch.ones(8192, dtype=torch.float64, device=cuda_device),
+                               atol=1e-5, rtol=0)
+    ls = K.log_softmax(x)
+    assert torch.isclose(ls.exp(), s, atol=1e-6, rtol=1e-5).all()
