@@ -51,6 +51,10 @@ KB_API int kb_version(void);                 /* MAJOR*10000 + MINOR*100 + PATCH 
 KB_API const char* kb_status_string(int status);
 KB_API const char* kb_last_error(void);      /* thread-local, never NULL */
 KB_API int kb_device_sm_count(int device);   /* streaming multiprocessors, or -1 */
+/* Device fault word of the current device: nonzero once a kernel gave up a
+ * bounded wait (a pipeline stalled for > 2 s) and returned early instead of
+ * hanging; its outputs are then invalid.  Synchronous; clear != 0 resets. */
+KB_API int kb_read_fault(int clear, int* value);
 
 /* ---- elementwise (y = f(x), n elements) ------------------------------- */
 /* replaces mingpt_gelu_entry, candidates/88_MinGPTNewGelu/v1.py:21-26

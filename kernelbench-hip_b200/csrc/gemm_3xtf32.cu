@@ -1,20 +1,623 @@
-// gemm_3xtf32.cu — placeholder entry points for the tcgen05 contractions.
+// gemm_3xtf32.cu — fp32 GEMM on the 5th-generation tensor cores (tcgen05)
+// with the 3xTF32 split, for square, batched and split-K shapes.
+//
+// fp32 accuracy from TF32 tensor cores: every operand element x is split into
+// hi = rna_tf32(x) (TF32 keeps 10 explicit mantissa bits) and lo = x - hi
+// (exact in fp32), and the product is accumulated in fp32 as
+//     C += A_lo * B_hi + A_hi * B_lo + A_hi * B_hi
+// (the A_lo * B_lo term is below fp32 resolution).  Because hi has its low 13
+// bits cleared, the result does not depend on whether the tensor core rounds
+// or truncates its fp32 inputs to TF32.
+//
+// Kernel structure (one CTA per 128 x BN output tile, 192 threads):
+//   warp 0      TMA producer: cp.async.bulk.tensor loads of the A tile
+//               (128 x 32, K-major, 128B swizzle) and of the B tile
+//               (32 x BN, N-major, 32-column boxes) into an S-stage ring,
+//               completion tracked by mbarrier transaction counts.
+//   warps 2-5   split converters: rewrite each landed stage in place as the
+//               hi part and write the lo part to the stage's lo buffers
+//               (element-wise, so the swizzled layout is preserved), then
+//               fence the generic->async proxy and arrive on conv[s].
+//   warp 1      allocates the TMEM accumulator (BN columns x 128 lanes) and
+//               one elected lane issues 12 tcgen05.mma.kind::tf32 (4 K-steps
+//               x 3 products) per stage; tcgen05.commit frees the stage.
+//   warps 2-5   epilogue: tcgen05.ld the accumulator lane quarter each warp
+//               owns and store fp32 C (or the split-K partial tile).
+// Every mbarrier wait is bounded (%globaltimer); on expiry the CTA raises a
+// shared abort flag and a device fault word, all roles leave their loops,
+// outstanding TMA loads are drained (bounded) and TMEM is freed.
+//
+// Shapes the TMA path cannot describe (row strides not multiples of 16 bytes,
+// unaligned bases) take a CUDA-core fp32 kernel.
+#include <cuda.h>
+
 #include "kb_common.cuh"
+
+namespace kb {
+
+__device__ int g_gemm_fault = 0;  // nonzero after a CTA gave up waiting
+
+namespace gemm {
+
+constexpr int BM = 128;
+constexpr int BK = 32;               // fp32 elements = one 128-byte swizzle row
+constexpr int kThreads = 192;
+constexpr int kConvThreads = 128;    // warps 2..5
+constexpr uint64_t kWaitLimitNs = 2000000000ull;
+
+template <int BN>
+struct Cfg {
+  static constexpr int S = (BN == 256) ? 2 : 3;
+  static constexpr int A_BYTES = BM * BK * 4;
+  static constexpr int B_BYTES = BN * BK * 4;
+  static constexpr int STAGE_BYTES = 2 * (A_BYTES + B_BYTES);   // hi + lo buffers
+  static constexpr int BAR_BYTES = 256;
+  static constexpr int SMEM_BYTES = S * STAGE_BYTES + BAR_BYTES + 1024;  // + alignment slack
+};
+
+// ------------------------------------------------------------------ PTX wrappers
+__device__ __forceinline__ uint32_t smem_u32(const void* p) {
+  return static_cast<uint32_t>(__cvta_generic_to_shared(p));
+}
+__device__ __forceinline__ uint64_t globaltimer() {
+  uint64_t t;
+  asm volatile("mov.u64 %0, %%globaltimer;" : "=l"(t));
+  return t;
+}
+__device__ __forceinline__ void mbar_init(uint32_t bar, uint32_t count) {
+  asm volatile("mbarrier.init.shared::cta.b64 [%0], %1;" ::"r"(bar), "r"(count) : "memory");
+}
+__device__ __forceinline__ void mbar_expect_tx(uint32_t bar, uint32_t bytes) {
+  asm volatile("mbarrier.arrive.expect_tx.shared::cta.b64 _, [%0], %1;" ::"r"(bar), "r"(bytes)
+               : "memory");
+}
+__device__ __forceinline__ void mbar_arrive(uint32_t bar) {
+  asm volatile("mbarrier.arrive.shared::cta.b64 _, [%0];" ::"r"(bar) : "memory");
+}
+__device__ __forceinline__ bool mbar_try_wait(uint32_t bar, uint32_t parity) {
+  uint32_t ok;
+  asm volatile(
+      "{\n\t.reg .pred p;\n\t"
+      "mbarrier.try_wait.parity.shared::cta.b64 p, [%1], %2;\n\t"
+      "selp.u32 %0, 1, 0, p;\n\t}"
+      : "=r"(ok)
+      : "r"(bar), "r"(parity)
+      : "memory");
+  return ok != 0;
+}
+// Bounded wait: false once the CTA (or any CTA of the launch) has aborted, or
+// after kWaitLimitNs without progress.
+__device__ __forceinline__ bool mbar_wait(uint32_t bar, uint32_t parity, volatile int* abort_flag) {
+  if (mbar_try_wait(bar, parity)) return true;
+  const uint64_t t0 = globaltimer();
+  for (uint32_t n = 1;; ++n) {
+    if (mbar_try_wait(bar, parity)) return true;
+    if ((n & 63) == 0) {
+      if (*abort_flag || *(volatile int*)&g_gemm_fault) {
+        *abort_flag = 1;
+        return false;
+      }
+      if (globaltimer() - t0 > kWaitLimitNs) {
+        *abort_flag = 1;
+        atomicExch(&g_gemm_fault, 1);
+        return false;
+      }
+    }
+  }
+}
+__device__ __forceinline__ void tma_load_3d(uint32_t dst, const CUtensorMap* tm, uint32_t bar, int c0,
+                                            int c1, int c2) {
+  asm volatile(
+      "cp.async.bulk.tensor.3d.shared::cluster.global.mbarrier::complete_tx::bytes "
+      "[%0], [%1, {%3, %4, %5}], [%2];" ::"r"(dst),
+      "l"(reinterpret_cast<uint64_t>(tm)), "r"(bar), "r"(c0), "r"(c1), "r"(c2)
+      : "memory");
+}
+__device__ __forceinline__ void fence_proxy_async() {
+  asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
+}
+__device__ __forceinline__ void fence_barrier_init() {
+  asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
+}
+__device__ __forceinline__ void tc_fence_before() {
+  asm volatile("tcgen05.fence::before_thread_sync;" ::: "memory");
+}
+__device__ __forceinline__ void tc_fence_after() {
+  asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory");
+}
+__device__ __forceinline__ void tmem_alloc(uint32_t dst_smem, uint32_t ncols) {
+  asm volatile("tcgen05.alloc.cta_group::1.sync.aligned.shared::cta.b32 [%0], %1;" ::"r"(dst_smem),
+               "r"(ncols)
+               : "memory");
+}
+__device__ __forceinline__ void tmem_relinquish() {
+  asm volatile("tcgen05.relinquish_alloc_permit.cta_group::1.sync.aligned;" ::: "memory");
+}
+__device__ __forceinline__ void tmem_dealloc(uint32_t taddr, uint32_t ncols) {
+  asm volatile("tcgen05.dealloc.cta_group::1.sync.aligned.b32 %0, %1;" ::"r"(taddr), "r"(ncols)
+               : "memory");
+}
+__device__ __forceinline__ void mma_tf32(uint32_t d_tmem, uint64_t a_desc, uint64_t b_desc,
+                                         uint32_t idesc, uint32_t accumulate) {
+  asm volatile(
+      "{\n\t.reg .pred p;\n\t"
+      "setp.ne.b32 p, %4, 0;\n\t"
+      "tcgen05.mma.cta_group::1.kind::tf32 [%0], %1, %2, %3, p;\n\t}" ::"r"(d_tmem),
+      "l"(a_desc), "l"(b_desc), "r"(idesc), "r"(accumulate)
+      : "memory");
+}
+__device__ __forceinline__ void mma_commit(uint32_t bar) {
+  asm volatile("tcgen05.commit.cta_group::1.mbarrier::arrive::one.shared::cluster.b64 [%0];" ::"r"(bar)
+               : "memory");
+}
+__device__ __forceinline__ void tmem_ld32(uint32_t taddr, uint32_t (&r)[32]) {
+  asm volatile(
+      "tcgen05.ld.sync.aligned.32x32b.x32.b32 "
+      "{%0, %1, %2, %3, %4, %5, %6, %7, %8, %9, %10, %11, %12, %13, %14, %15, "
+      "%16, %17, %18, %19, %20, %21, %22, %23, %24, %25, %26, %27, %28, %29, %30, %31}, [%32];"
+      : "=r"(r[0]), "=r"(r[1]), "=r"(r[2]), "=r"(r[3]), "=r"(r[4]), "=r"(r[5]), "=r"(r[6]),
+        "=r"(r[7]), "=r"(r[8]), "=r"(r[9]), "=r"(r[10]), "=r"(r[11]), "=r"(r[12]), "=r"(r[13]),
+        "=r"(r[14]), "=r"(r[15]), "=r"(r[16]), "=r"(r[17]), "=r"(r[18]), "=r"(r[19]),
+        "=r"(r[20]), "=r"(r[21]), "=r"(r[22]), "=r"(r[23]), "=r"(r[24]), "=r"(r[25]),
+        "=r"(r[26]), "=r"(r[27]), "=r"(r[28]), "=r"(r[29]), "=r"(r[30]), "=r"(r[31])
+      : "r"(taddr));
+}
+__device__ __forceinline__ void tmem_ld_wait() {
+  asm volatile("tcgen05.wait::ld.sync.aligned;" ::: "memory");
+}
+__device__ __forceinline__ float tf32_rna(float x) {
+  uint32_t r;
+  asm("cvt.rna.tf32.f32 %0, %1;" : "=r"(r) : "f"(x));
+  return __uint_as_float(r);
+}
+
+// UMMA shared-memory descriptor, 128-byte swizzle (layout type 2), version 1.
+// K-major:  LBO unused (16 B), SBO = 1024 B between 8-row groups.
+// MN-major: LBO = byte stride between 32-element (128 B) column blocks,
+//           SBO = 1024 B between 8-row K groups.
+__device__ __forceinline__ uint64_t make_desc(uint32_t saddr, uint32_t lbo, uint32_t sbo) {
+  uint64_t d = 0;
+  d |= (uint64_t)((saddr >> 4) & 0x3FFFu);
+  d |= (uint64_t)((lbo >> 4) & 0x3FFFu) << 16;
+  d |= (uint64_t)((sbo >> 4) & 0x3FFFu) << 32;
+  d |= (uint64_t)1 << 46;  // descriptor version for tcgen05
+  d |= (uint64_t)2 << 61;  // SWIZZLE_128B
+  return d;
+}
+
+// Instruction descriptor: D f32, A/B tf32, A K-major or MN-major, B MN-major.
+__host__ __device__ constexpr uint32_t make_idesc(int M, int N, bool a_mn) {
+  return (1u << 4) | (2u << 7) | (2u << 10) | ((a_mn ? 1u : 0u) << 15) | (1u << 16) |
+         ((uint32_t)(N >> 3) << 17) | ((uint32_t)(M >> 4) << 24);
+}
+
+// Split the float4s [begin, n4) (stride kConvThreads) of `buf` in place into
+// hi and write lo to `lo`.  Non-finite inputs keep hi = x, lo = 0.
+__device__ __forceinline__ void split_buffer(float4* buf, float4* lo, int n4, int t) {
+#pragma unroll 4
+  for (int i = t; i < n4; i += kConvThreads) {
+    float4 v = buf[i], h, l;
+    h.x = tf32_rna(v.x); h.y = tf32_rna(v.y); h.z = tf32_rna(v.z); h.w = tf32_rna(v.w);
+    l.x = v.x - h.x; l.y = v.y - h.y; l.z = v.z - h.z; l.w = v.w - h.w;
+    if (!isfinite(l.x)) { h.x = v.x; l.x = 0.f; }
+    if (!isfinite(l.y)) { h.y = v.y; l.y = 0.f; }
+    if (!isfinite(l.z)) { h.z = v.z; l.z = 0.f; }
+    if (!isfinite(l.w)) { h.w = v.w; l.w = 0.f; }
+    buf[i] = h;
+    lo[i] = l;
+  }
+}
+
+struct Params {
+  float* C;          // output (mode 0) or partial tiles [Z][M][N] (mode 1)
+  int M, N, K;
+  int64_t ldc;
+  int64_t batch_stride_c;
+  int kb_per_split;  // mode 1: k-blocks per split
+  int mode;          // 0: z = batch index, 1: z = split index (write partials)
+};
+
+template <int BN, bool TRANS_A>
+__global__ void __launch_bounds__(kThreads, 1)
+gemm3x_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUtensorMap tmB, Params p) {
+  using CF = Cfg<BN>;
+  constexpr int S = CF::S;
+  extern __shared__ uint8_t smem_raw[];
+  uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
+  uint64_t* bars = reinterpret_cast<uint64_t*>(smem + S * CF::STAGE_BYTES);
+  // bars[0..S) full, [S..2S) conv, [2S..3S) empty, [3S] acc
+  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(bars + 3 * S + 1);
+  volatile int* abort_flag = reinterpret_cast<volatile int*>(tmem_slot + 1);
+
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const int n0 = blockIdx.x * BN, m0 = blockIdx.y * BM;
+  const int z = blockIdx.z;
+  const int nk_total = (p.K + BK - 1) / BK;
+  int kb_begin = 0, kb_end = nk_total, batch = z;
+  if (p.mode == 1) {
+    kb_begin = z * p.kb_per_split;
+    kb_end = min(nk_total, kb_begin + p.kb_per_split);
+    batch = 0;
+  }
+  const int nk = max(kb_end - kb_begin, 0);
+
+  auto full = [&](int s) { return smem_u32(bars + s); };
+  auto conv = [&](int s) { return smem_u32(bars + S + s); };
+  auto empty = [&](int s) { return smem_u32(bars + 2 * S + s); };
+  const uint32_t acc_bar = smem_u32(bars + 3 * S);
+
+  if (threadIdx.x == 0) {
+    for (int s = 0; s < S; ++s) {
+      mbar_init(full(s), 1);
+      mbar_init(conv(s), kConvThreads);
+      mbar_init(empty(s), 1);
+    }
+    mbar_init(acc_bar, 1);
+    *abort_flag = 0;
+    fence_barrier_init();
+  }
+  if (warp == 1) {
+    tmem_alloc(smem_u32(tmem_slot), BN);
+    tmem_relinquish();
+  }
+  tc_fence_before();
+  __syncthreads();
+  tc_fence_after();
+  const uint32_t tmem = *tmem_slot;
+
+  auto stage_ptr = [&](int s) { return smem + s * CF::STAGE_BYTES; };
+
+  if (warp == 0) {
+    // ---------------- TMA producer
+    if (lane == 0) {
+      int issued = 0;
+      for (int it = 0; it < nk; ++it) {
+        const int s = it % S;
+        if (!mbar_wait(empty(s), ((it / S) & 1) ^ 1, abort_flag)) break;
+        uint8_t* st = stage_ptr(s);
+        const int k0 = (kb_begin + it) * BK;
+        mbar_expect_tx(full(s), CF::A_BYTES + CF::B_BYTES);
+        if (TRANS_A) {
+#pragma unroll
+          for (int j = 0; j < BM / 32; ++j)
+            tma_load_3d(smem_u32(st + j * 4096), &tmA, full(s), m0 + 32 * j, k0, batch);
+        } else {
+          tma_load_3d(smem_u32(st), &tmA, full(s), k0, m0, batch);
+        }
+#pragma unroll
+        for (int j = 0; j < BN / 32; ++j)
+          tma_load_3d(smem_u32(st + CF::A_BYTES + j * 4096), &tmB, full(s), n0 + 32 * j, k0, batch);
+        ++issued;
+      }
+      // drain: every issued load must land before the CTA may exit
+      for (int it = max(issued - S, 0); it < issued; ++it) {
+        const int s = it % S;
+        const uint64_t t0 = globaltimer();
+        while (!mbar_try_wait(full(s), (it / S) & 1)) {
+          if (globaltimer() - t0 > kWaitLimitNs) break;
+        }
+      }
+    }
+  } else if (warp == 1) {
+    // ---------------- MMA issuer
+    if (lane == 0) {
+      constexpr uint32_t idesc = make_idesc(BM, BN, TRANS_A);
+      for (int it = 0; it < nk; ++it) {
+        const int s = it % S;
+        if (!mbar_wait(conv(s), (it / S) & 1, abort_flag)) break;
+        tc_fence_after();
+        uint8_t* st = stage_ptr(s);
+        const uint32_t a_hi = smem_u32(st);
+        const uint32_t b_hi = a_hi + CF::A_BYTES;
+        const uint32_t a_lo = b_hi + CF::B_BYTES;
+        const uint32_t b_lo = a_lo + CF::A_BYTES;
+#pragma unroll
+        for (int kk = 0; kk < BK / 8; ++kk) {
+          // K step of 8 tf32: +32 B inside the K-major swizzle row, or +8 rows
+          // (1024 B) in the MN-major layout.
+          const uint32_t aoff = TRANS_A ? kk * 1024 : kk * 32;
+          const uint32_t boff = kk * 1024;
+          const uint64_t dah = TRANS_A ? make_desc(a_hi + aoff, 4096, 1024) : make_desc(a_hi + aoff, 16, 1024);
+          const uint64_t dal = TRANS_A ? make_desc(a_lo + aoff, 4096, 1024) : make_desc(a_lo + aoff, 16, 1024);
+          const uint64_t dbh = make_desc(b_hi + boff, 4096, 1024);
+          const uint64_t dbl = make_desc(b_lo + boff, 4096, 1024);
+          mma_tf32(tmem, dal, dbh, idesc, (it > 0 || kk > 0) ? 1u : 0u);
+          mma_tf32(tmem, dah, dbl, idesc, 1u);
+          mma_tf32(tmem, dah, dbh, idesc, 1u);
+        }
+        mma_commit(empty(s));
+      }
+      mma_commit(acc_bar);
+    }
+  } else {
+    // ---------------- split converters (warps 2..5)
+    const int t = threadIdx.x - 64;
+    for (int it = 0; it < nk; ++it) {
+      const int s = it % S;
+      if (!mbar_wait(full(s), (it / S) & 1, abort_flag)) break;
+      uint8_t* st = stage_ptr(s);
+      split_buffer(reinterpret_cast<float4*>(st), reinterpret_cast<float4*>(st + CF::A_BYTES + CF::B_BYTES),
+                   CF::A_BYTES / 16, t);
+      split_buffer(reinterpret_cast<float4*>(st + CF::A_BYTES),
+                   reinterpret_cast<float4*>(st + 2 * CF::A_BYTES + CF::B_BYTES), CF::B_BYTES / 16, t);
+      fence_proxy_async();
+      mbar_arrive(conv(s));
+    }
+    // ---------------- epilogue
+    // warp-uniform: tcgen05.ld below must be executed by all 32 lanes
+    const bool ok = __all_sync(0xffffffffu, (nk == 0) || mbar_wait(acc_bar, 0, abort_flag));
+    tc_fence_after();
+    const int q = warp & 3;  // TMEM lane quarter this warp may access
+    const int row = m0 + q * 32 + lane;
+    float* out = p.C + (int64_t)batch * p.batch_stride_c;
+    int64_t ldo = p.ldc;
+    if (p.mode == 1) {
+      out = p.C + (int64_t)z * p.M * p.N;
+      ldo = p.N;
+    }
+    float* orow = out + (int64_t)row * ldo;
+    const bool vec = ((ldo & 3) == 0) && ((reinterpret_cast<uintptr_t>(out) & 15) == 0);
+#pragma unroll 1
+    for (int c = 0; c < BN / 32; ++c) {
+      uint32_t r[32];
+      if (nk > 0 && ok) {
+        tmem_ld32(tmem + ((uint32_t)(q * 32) << 16) + c * 32, r);
+        tmem_ld_wait();
+      } else {
+#pragma unroll
+        for (int j = 0; j < 32; ++j) r[j] = 0u;
+      }
+      const int col0 = n0 + c * 32;
+      if (row < p.M && ok) {
+        if (vec && col0 + 32 <= p.N) {
+#pragma unroll
+          for (int j = 0; j < 32; j += 4)
+            *reinterpret_cast<float4*>(orow + col0 + j) =
+                make_float4(__uint_as_float(r[j]), __uint_as_float(r[j + 1]),
+                            __uint_as_float(r[j + 2]), __uint_as_float(r[j + 3]));
+        } else {
+#pragma unroll
+          for (int j = 0; j < 32; ++j)
+            if (col0 + j < p.N) orow[col0 + j] = __uint_as_float(r[j]);
+        }
+      }
+    }
+  }
+  tc_fence_before();
+  __syncthreads();
+  if (warp == 1) {
+    tc_fence_after();
+    tmem_dealloc(tmem, BN);
+  }
+}
+
+// deterministic split-K reduction: C[m, n] = sum_z partial[z][m][n], z in order
+__global__ void splitk_reduce_kernel(const float* __restrict__ part, float* __restrict__ C, int M, int N,
+                                     int64_t ldc, int Z) {
+  const int64_t total = (int64_t)M * N;
+  for (int64_t i = (int64_t)blockIdx.x * blockDim.x + threadIdx.x; i < total;
+       i += (int64_t)gridDim.x * blockDim.x) {
+    float s = 0.f;
+    for (int zz = 0; zz < Z; ++zz) s += part[(int64_t)zz * total + i];
+    const int64_t m = i / N, n = i - m * N;
+    C[m * ldc + n] = s;
+  }
+}
+
+// CUDA-core fp32 GEMM for shapes the TMA path cannot describe.
+__global__ void __launch_bounds__(256)
+gemm_simt_kernel(const float* __restrict__ A, const float* __restrict__ B, float* __restrict__ C, int M,
+                 int N, int K, int64_t lda, int64_t ldb, int64_t ldc, int64_t sA, int64_t sB, int64_t sC,
+                 int trans_a) {
+  __shared__ float As[16][17], Bs[16][17];
+  const int tx = threadIdx.x & 15, ty = threadIdx.x >> 4;
+  const int b = blockIdx.z;
+  A += b * sA;
+  B += b * sB;
+  C += b * sC;
+  const int row = blockIdx.y * 16 + ty, col = blockIdx.x * 16 + tx;
+  float acc = 0.f;
+  for (int k0 = 0; k0 < K; k0 += 16) {
+    const int ka = k0 + tx, kb = k0 + ty;
+    As[ty][tx] = (row < M && ka < K) ? (trans_a ? A[(int64_t)ka * lda + row] : A[(int64_t)row * lda + ka]) : 0.f;
+    Bs[ty][tx] = (kb < K && col < N) ? B[(int64_t)kb * ldb + col] : 0.f;
+    __syncthreads();
+#pragma unroll
+    for (int k = 0; k < 16; ++k) acc = fmaf(As[ty][k], Bs[k][tx], acc);
+    __syncthreads();
+  }
+  if (row < M && col < N) C[(int64_t)row * ldc + col] = acc;
+}
+
+// ------------------------------------------------------------------ host side
+using EncodeFn = CUresult (*)(CUtensorMap*, CUtensorMapDataType, cuuint32_t, void*, const cuuint64_t*,
+                              const cuuint64_t*, const cuuint32_t*, const cuuint32_t*, CUtensorMapInterleave,
+                              CUtensorMapSwizzle, CUtensorMapL2promotion, CUtensorMapFloatOOBfill);
+
+EncodeFn encode_fn() {
+  static EncodeFn fn = nullptr;
+  if (!fn) {
+    void* p = nullptr;
+    cudaDriverEntryPointQueryResult q;
+    if (cudaGetDriverEntryPoint("cuTensorMapEncodeTiled", &p, cudaEnableDefault, &q) == cudaSuccess &&
+        q == cudaDriverEntryPointSuccess)
+      fn = reinterpret_cast<EncodeFn>(p);
+  }
+  return fn;
+}
+
+// 3-D fp32 tensor map {inner, outer, batch}, box {32, box_outer, 1}, 128B swizzle.
+int make_map(CUtensorMap* tm, const float* base, int64_t inner, int64_t outer, int64_t batch,
+             int64_t row_stride_elems, int64_t batch_stride_elems, int box_outer) {
+  EncodeFn enc = encode_fn();
+  KB_REQUIRE(enc != nullptr, KB_ERR_CUDA, "cuTensorMapEncodeTiled unavailable");
+  cuuint64_t dims[3] = {(cuuint64_t)inner, (cuuint64_t)outer, (cuuint64_t)batch};
+  cuuint64_t strides[2] = {(cuuint64_t)row_stride_elems * 4, (cuuint64_t)batch_stride_elems * 4};
+  cuuint32_t box[3] = {32, (cuuint32_t)box_outer, 1};
+  cuuint32_t estr[3] = {1, 1, 1};
+  CUresult r = enc(tm, CU_TENSOR_MAP_DATA_TYPE_FLOAT32, 3, const_cast<float*>(base), dims, strides, box, estr,
+                   CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B,
+                   CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+  KB_REQUIRE(r == CUDA_SUCCESS, KB_ERR_CUDA, "cuTensorMapEncodeTiled failed (%d)", (int)r);
+  return KB_OK;
+}
+
+template <int BN, bool TA>
+int launch_tc(const CUtensorMap& ta, const CUtensorMap& tb, const Params& p, dim3 grid, cudaStream_t s) {
+  auto kern = gemm3x_kernel<BN, TA>;
+  static uint64_t attr_set = 0;  // one bit per device ordinal
+  int dev = 0;
+  KB_CUDA(cudaGetDevice(&dev));
+  if (dev < 64 && !(attr_set >> dev & 1)) {
+    KB_CUDA(cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, Cfg<BN>::SMEM_BYTES));
+    attr_set |= 1ull << dev;
+  }
+  kern<<<grid, kThreads, Cfg<BN>::SMEM_BYTES, s>>>(ta, tb, p);
+  return check_launch("gemm3x_kernel");
+}
+
+struct GemmArgs {
+  const float* A;
+  const float* B;
+  float* C;
+  int64_t batch, M, N, K, lda, ldb, ldc, sA, sB, sC;
+  bool trans_a;
+};
+
+bool tma_ok(const GemmArgs& g) {
+  auto a16 = [](int64_t v) { return (v * 4) % 16 == 0; };
+  return aligned16(g.A) && aligned16(g.B) && a16(g.lda) && a16(g.ldb) && a16(g.sA) && a16(g.sB) &&
+         g.M < (1LL << 31) && g.N < (1LL << 31) && g.K < (1LL << 31) && g.K > 0 && g.batch <= 65535 &&
+         (g.trans_a ? g.M : g.K) >= 4 && g.N >= 4;
+}
+
+int run_simt(const GemmArgs& g, cudaStream_t s) {
+  KB_REQUIRE(g.batch <= 65535, KB_ERR_UNSUPPORTED, "batch > 65535");
+  dim3 grid((unsigned)ceil_div(g.N, 16), (unsigned)ceil_div(g.M, 16), (unsigned)g.batch);
+  gemm_simt_kernel<<<grid, 256, 0, s>>>(g.A, g.B, g.C, (int)g.M, (int)g.N, (int)g.K, g.lda, g.ldb, g.ldc,
+                                        g.sA, g.sB, g.sC, g.trans_a ? 1 : 0);
+  return check_launch("gemm_simt_kernel");
+}
+
+// splits > 1: partial tiles go to `ws` and are reduced into C afterwards.
+int run_gemm(const GemmArgs& g, int splits, float* ws, cudaStream_t s) {
+  if (g.M == 0 || g.N == 0 || g.batch == 0) return KB_OK;
+  if (!tma_ok(g)) return run_simt(g, s);
+  const bool bn256 = g.N > 128;
+  const int BN = bn256 ? 256 : 128;
+  CUtensorMap ta, tb;
+  if (g.trans_a) {
+    if (int st = make_map(&ta, g.A, g.M, g.K, g.batch, g.lda, g.sA, 32)) return st;
+  } else {
+    if (int st = make_map(&ta, g.A, g.K, g.M, g.batch, g.lda, g.sA, BM)) return st;
+  }
+  if (int st = make_map(&tb, g.B, g.N, g.K, g.batch, g.ldb, g.sB, 32)) return st;
+  const int nk = (int)ceil_div(g.K, BK);
+  Params p{};
+  p.M = (int)g.M;
+  p.N = (int)g.N;
+  p.K = (int)g.K;
+  dim3 grid((unsigned)ceil_div(g.N, BN), (unsigned)ceil_div(g.M, BM), 1);
+  if (splits > 1) {
+    const int kbps = (int)ceil_div(nk, splits);
+    splits = (int)ceil_div(nk, kbps);  // no empty split
+    p.C = ws;
+    p.ldc = g.N;
+    p.mode = 1;
+    p.kb_per_split = kbps;
+    grid.z = splits;
+  } else {
+    p.C = g.C;
+    p.ldc = g.ldc;
+    p.batch_stride_c = g.sC;
+    p.mode = 0;
+    grid.z = (unsigned)g.batch;
+  }
+  int st;
+  if (bn256)
+    st = g.trans_a ? launch_tc<256, true>(ta, tb, p, grid, s) : launch_tc<256, false>(ta, tb, p, grid, s);
+  else
+    st = g.trans_a ? launch_tc<128, true>(ta, tb, p, grid, s) : launch_tc<128, false>(ta, tb, p, grid, s);
+  if (st) return st;
+  if (splits > 1) {
+    const int64_t total = g.M * g.N;
+    const int blocks = (int)std::min<int64_t>(ceil_div(total, 256), (int64_t)sm_count() * 8);
+    splitk_reduce_kernel<<<blocks, 256, 0, s>>>(ws, g.C, (int)g.M, (int)g.N, g.ldc, splits);
+    return check_launch("splitk_reduce_kernel");
+  }
+  return KB_OK;
+}
+
+constexpr int kMaxSms = 160;
+
+int splitk_count(int64_t M, int64_t N, int64_t K, int sms) {
+  const int64_t tiles = ceil_div(M, BM) * ceil_div(N, N > 128 ? 256 : 128);
+  const int64_t nk = ceil_div(K, BK);
+  int64_t sp = std::max<int64_t>(1, sms / std::max<int64_t>(tiles, 1));
+  sp = std::min<int64_t>(sp, std::max<int64_t>(nk / 4, 1));  // at least 4 k-blocks per split
+  return (int)sp;
+}
+
+}  // namespace gemm
+}  // namespace kb
 
 extern "C" {
 
-int kb_sgemm_3xtf32(const float*, const float*, float*, int64_t, int64_t, int64_t, int64_t,
-                    int64_t, int64_t, int, kbStream) {
-  return kb::set_error(KB_ERR_UNSUPPORTED, "kb_sgemm_3xtf32: not built yet");
+int kb_read_fault(int clear, int* value) {
+  KB_REQUIRE(value, KB_ERR_INVALID_ARG, "kb_read_fault: null pointer");
+  KB_CUDA(cudaMemcpyFromSymbol(value, kb::g_gemm_fault, sizeof(int)));
+  if (clear) {
+    const int zero = 0;
+    KB_CUDA(cudaMemcpyToSymbol(kb::g_gemm_fault, &zero, sizeof(int)));
+  }
+  return KB_OK;
 }
-int kb_bgemm_3xtf32(const float*, const float*, float*, int64_t, int64_t, int64_t, int64_t,
-                    kbStream) {
-  return kb::set_error(KB_ERR_UNSUPPORTED, "kb_bgemm_3xtf32: not built yet");
+
+int kb_sgemm_3xtf32(const float* A, const float* B, float* C, int64_t M, int64_t N, int64_t K,
+                    int64_t lda, int64_t ldb, int64_t ldc, int trans_a, kbStream stream) {
+  KB_REQUIRE(M >= 0 && N >= 0 && K >= 0, KB_ERR_INVALID_ARG, "kb_sgemm_3xtf32: negative size");
+  if (M == 0 || N == 0) return KB_OK;
+  KB_REQUIRE(A && B && C, KB_ERR_INVALID_ARG, "kb_sgemm_3xtf32: null pointer");
+  KB_REQUIRE(lda >= (trans_a ? M : K) && ldb >= N && ldc >= N, KB_ERR_INVALID_ARG,
+             "kb_sgemm_3xtf32: leading dimension too small");
+  kb::gemm::GemmArgs g{A, B, C, 1, M, N, K, lda, ldb, ldc, 0, 0, 0, trans_a != 0};
+  g.sA = lda * (trans_a ? K : M);
+  g.sB = ldb * K;
+  g.sC = ldc * M;
+  return kb::gemm::run_gemm(g, 1, nullptr, stream);
 }
-size_t kb_gemm_splitk_workspace_size(int64_t, int64_t, int64_t) { return 0; }
-int kb_gemm_splitk_3xtf32(const float*, const float*, float*, int64_t, int64_t, int64_t, void*,
-                          size_t, kbStream) {
-  return kb::set_error(KB_ERR_UNSUPPORTED, "kb_gemm_splitk_3xtf32: not built yet");
+
+int kb_bgemm_3xtf32(const float* A, const float* B, float* C, int64_t batch, int64_t M, int64_t N,
+                    int64_t K, kbStream stream) {
+  KB_REQUIRE(batch >= 0 && M >= 0 && N >= 0 && K >= 0, KB_ERR_INVALID_ARG, "kb_bgemm_3xtf32: negative size");
+  if (batch == 0 || M == 0 || N == 0) return KB_OK;
+  KB_REQUIRE(A && B && C, KB_ERR_INVALID_ARG, "kb_bgemm_3xtf32: null pointer");
+  KB_REQUIRE(batch <= 65535, KB_ERR_UNSUPPORTED, "kb_bgemm_3xtf32: batch > 65535");
+  kb::gemm::GemmArgs g{A, B, C, batch, M, N, K, K, N, N, M * K, K * N, M * N, false};
+  return kb::gemm::run_gemm(g, 1, nullptr, stream);
+}
+
+size_t kb_gemm_splitk_workspace_size(int64_t M, int64_t N, int64_t K) {
+  const int sp = kb::gemm::splitk_count(M, N, K, kb::gemm::kMaxSms);
+  return sp > 1 ? (size_t)sp * M * N * sizeof(float) : 0;
+}
+
+int kb_gemm_splitk_3xtf32(const float* A, const float* B, float* C, int64_t M, int64_t N, int64_t K,
+                          void* workspace, size_t workspace_bytes, kbStream stream) {
+  const char* name = "kb_gemm_splitk_3xtf32";
+  KB_REQUIRE(M >= 0 && N >= 0 && K >= 0, KB_ERR_INVALID_ARG, "%s: negative size", name);
+  if (M == 0 || N == 0) return KB_OK;
+  KB_REQUIRE(A && B && C, KB_ERR_INVALID_ARG, "%s: null pointer", name);
+  kb::gemm::GemmArgs g{A, B, C, 1, M, N, K, K, N, N, M * K, K * N, M * N, false};
+  int sp = kb::gemm::splitk_count(M, N, K, kb::sm_count());
+  if (sp > 1) {
+    const size_t need = (size_t)sp * M * N * sizeof(float);
+    KB_REQUIRE(workspace && workspace_bytes >= need, KB_ERR_WORKSPACE,
+               "%s: workspace of %zu bytes needed, %zu given", name, need, workspace_bytes);
+    KB_REQUIRE(kb::aligned16(workspace), KB_ERR_INVALID_ARG, "%s: workspace must be 16-byte aligned", name);
+    if (!kb::gemm::tma_ok(g)) sp = 1;
+  }
+  return kb::gemm::run_gemm(g, sp, static_cast<float*>(workspace), stream);
 }
 
 }  // extern "C"

@@ -214,7 +214,12 @@ __global__ void __launch_bounds__(NT) row_block_kernel(RowArgs a) {
   }
   ClusterReducer<NT, CL> r{red, slots};
   row_math<OP, VPT>(v, ok, a, ys, col4_base, NT, threadIdx.x, r);
-  if constexpr (CL > 1) cg::this_cluster().sync();  // peers may still read `slots`
+  // Peers may still read `slots` through DSMEM: wait for the whole cluster
+  // before this CTA's shared memory goes away.  Relaxed arrive — the row's
+  // global stores need no cluster-scope release, and a releasing barrier
+  // would stall on them.
+  if constexpr (CL > 1)
+    asm volatile("barrier.cluster.arrive.relaxed.aligned;\n\tbarrier.cluster.wait.aligned;" ::: "memory");
 }
 
 // One warp per row (rows of at most 32 * VPT * 4 floats); 4 warps per CTA.

@@ -26,6 +26,7 @@ SIGNATURES: dict[str, tuple] = {
     "kb_status_string": (C.c_char_p, [_int]),
     "kb_last_error": (C.c_char_p, []),
     "kb_device_sm_count": (_int, [_int]),
+    "kb_read_fault": (_int, [_int, C.POINTER(C.c_int)]),
     "kb_gelu_tanh_f32": (_int, [_p, _p, _i64, _p]),
     "kb_gelu_erf_f32": (_int, [_p, _p, _i64, _p]),
     "kb_swish_f32": (_int, [_p, _p, _i64, _p]),
@@ -86,6 +87,13 @@ def check(fn_name: str, status: int) -> None:
     if status != 0:
         msg = LIB.kb_last_error().decode(errors="replace")
         raise KbError(fn_name, status, msg)
+
+
+def read_fault(clear: bool = True) -> int:
+    """Device fault word (nonzero if a kernel abandoned a bounded wait)."""
+    v = C.c_int(0)
+    check("kb_read_fault", LIB.kb_read_fault(1 if clear else 0, C.byref(v)))
+    return v.value
 
 
 def exported_symbols() -> list[str]:

@@ -292,3 +292,104 @@ def test_full_size_row_sums(cuda_device):
                                atol=1e-5, rtol=0)
     ls = K.log_softmax(x)
     assert torch.isclose(ls.exp(), s, atol=1e-6, rtol=1e-5).all()
+
+
+# ------------------------------------------------------------ tcgen05 contractions
+def _gemm_check(got, A, B, what, trans=False, batched=False, tol=1e-5):
+    """Error relative to sum |a||b| (the natural scale of a dot product): 3xTF32
+    holds it near fp32 rounding; a single TF32 pass would sit near 1e-3."""
+    Ad, Bd = A.double(), B.double()
+    if trans:
+        Ad = Ad.transpose(-1, -2)
+    ref = Ad @ Bd
+    scale = Ad.abs() @ Bd.abs()
+    err = ((got.double() - ref).abs() / scale.clamp_min(1e-300)).max().item()
+    assert err < tol, f"{what}: relative error {err:.3e}"
+
+
+@pytest.mark.parametrize("mnk", [(128, 256, 32), (256, 256, 64), (300, 520, 100), (128, 128, 96),
+                                 (1024, 1024, 1024), (2048, 1536, 2048), (129, 257, 33), (64, 40, 8)])
+def test_sgemm_shapes(mnk, cuda_device):
+    from kbb200 import ops as K
+    from kbb200._lib import read_fault
+
+    M, N, Kd = mnk
+    g = torch.Generator(device=cuda_device).manual_seed(M + N + Kd)
+    A = torch.randn(M, Kd, device=cuda_device, generator=g)
+    B = torch.randn(Kd, N, device=cuda_device, generator=g)
+    _gemm_check(K.matmul(A, B), A, B, f"sgemm {mnk}")
+    assert read_fault() == 0
+
+
+@pytest.mark.parametrize("mnk", [(512, 384, 256), (130, 260, 68)])
+def test_sgemm_transposed_a(mnk, cuda_device):
+    from kbb200 import ops as K
+
+    M, N, Kd = mnk
+    At = torch.randn(Kd, M, device=cuda_device)          # A stored as [K, M]
+    B = torch.randn(Kd, N, device=cuda_device)
+    _gemm_check(K.matmul(At, B, trans_a=True), At, B, f"sgemm^T {mnk}", trans=True)
+
+
+def test_sgemm_odd_strides_use_cuda_core_path(cuda_device):
+    from kbb200 import ops as K
+
+    A = torch.randn(33, 77, device=cuda_device)
+    B = torch.randn(77, 65, device=cuda_device)
+    _gemm_check(K.matmul(A, B), A, B, "odd sgemm")
+
+
+@pytest.mark.parametrize("shape", [(4, 256, 384, 512), (3, 128, 96, 256), (2, 130, 70, 40)])
+def test_bmm_shapes(shape, cuda_device):
+    from kbb200 import ops as K
+
+    bt, M, N, Kd = shape
+    A = torch.randn(bt, M, Kd, device=cuda_device)
+    B = torch.randn(bt, Kd, N, device=cuda_device)
+    _gemm_check(K.bmm(A, B), A, B, f"bmm {shape}", batched=True)
+
+
+@pytest.mark.parametrize("mnk", [(256, 256, 65536), (200, 72, 20000), (256, 256, 4096)])
+def test_splitk_shapes(mnk, cuda_device):
+    from kbb200 import ops as K
+    from kbb200._lib import read_fault
+
+    M, N, Kd = mnk
+    A = torch.randn(M, Kd, device=cuda_device)
+    B = torch.randn(Kd, N, device=cuda_device)
+    C = K.matmul_splitk(A, B)
+    _gemm_check(C, A, B, f"splitk {mnk}")
+    assert torch.equal(C, K.matmul_splitk(A, B)), "split-K must be deterministic"
+    assert read_fault() == 0
+
+
+def test_gemm_special_values(cuda_device):
+    from kbb200 import ops as K
+
+    A = torch.randn(128, 64, device=cuda_device)
+    B = torch.randn(64, 256, device=cuda_device)
+    A[3, 5] = float("inf")
+    B[7, 9] = float("nan")
+    got = K.matmul(A, B)
+    want = (A.double() @ B.double()).float()
+    assert torch.equal(torch.isnan(got), torch.isnan(want))
+    assert torch.equal(torch.isinf(got), torch.isinf(want))
+
+
+@pytest.mark.parametrize("name", sorted(GEMMS))
+def test_gemm_full_size_vs_torch_fp32(name, cuda_device):
+    """Benchmark shapes against torch's fp32 (non-TF32) matmul, atol=rtol=1e-3."""
+    from kbb200.workloads import WORKLOADS, make_inputs
+
+    w = next(w for w in WORKLOADS.values() if w.problem == name)
+    A, B = make_inputs(w, cuda_device, seed=0)
+    got = gpu_call(name)(A, B)
+    prev = torch.backends.cuda.matmul.allow_tf32
+    torch.backends.cuda.matmul.allow_tf32 = False
+    try:
+        want = torch.bmm(A, B) if A.dim() == 3 else A @ B
+    finally:
+        torch.backends.cuda.matmul.allow_tf32 = prev
+    assert torch.isclose(got, want, atol=1e-3, rtol=1e-3).all()
+    del A, B, got, want
+    torch.cuda.empty_cache()
