@@ -12,7 +12,8 @@
 // Kernel structure (one CTA per 128 x BN output tile, 192 threads):
 //   warp 0      TMA producer: cp.async.bulk.tensor loads of the A tile
 //               (128 x 32, K-major, 128B swizzle) and of the B tile
-//               (32 x BN, N-major, 32-column boxes) into an S-stage ring,
+//               (32 x BN, N-major, 32-column boxes, 128B swizzle with
+//               32-byte atoms) into an S-stage ring,
 //               completion tracked by mbarrier transaction counts.
 //   warps 2-5   split converters: rewrite each landed stage in place as the
 //               hi part and write the lo part to the stage's lo buffers
@@ -171,18 +172,32 @@ __device__ __forceinline__ float tf32_rna(float x) {
   return __uint_as_float(r);
 }
 
-// UMMA shared-memory descriptor, 128-byte swizzle (layout type 2), version 1.
-// K-major:  LBO unused (16 B), SBO = 1024 B between 8-row groups.
-// MN-major: LBO = byte stride between 32-element (128 B) column blocks,
-//           SBO = 1024 B between 8-row K groups.
-__device__ __forceinline__ uint64_t make_desc(uint32_t saddr, uint32_t lbo, uint32_t sbo) {
+// UMMA shared-memory descriptors (version 1).  TF32 operands come in two
+// canonical layouts, matching how TMA writes them:
+//   K-major  (A as stored [M, K]): 128-byte swizzle with 16-byte atoms
+//            (layout type 2); 8-row groups of 128-byte rows, SBO = 1024 B,
+//            LBO unused.  A K step of 8 tf32 advances the start by 32 B.
+//   MN-major (B [K, N], and A stored [K, M]): TF32 accepts only the 128-byte
+//            swizzle with 32-byte atoms (layout type 1): 4-row groups of
+//            128-byte rows, SBO = 512 B between groups, LBO = 4096 B between
+//            the 32-element column blocks (one TMA box each).  A K step of 8
+//            rows advances the start by 1024 B.
+constexpr uint32_t kLayoutSw128 = 2;
+constexpr uint32_t kLayoutSw128Atom32 = 1;
+__device__ __forceinline__ uint64_t make_desc(uint32_t saddr, uint32_t lbo, uint32_t sbo, uint32_t layout) {
   uint64_t d = 0;
   d |= (uint64_t)((saddr >> 4) & 0x3FFFu);
   d |= (uint64_t)((lbo >> 4) & 0x3FFFu) << 16;
   d |= (uint64_t)((sbo >> 4) & 0x3FFFu) << 32;
   d |= (uint64_t)1 << 46;  // descriptor version for tcgen05
-  d |= (uint64_t)2 << 61;  // SWIZZLE_128B
+  d |= (uint64_t)layout << 61;
   return d;
+}
+__device__ __forceinline__ uint64_t desc_kmajor(uint32_t saddr) {
+  return make_desc(saddr, 16, 1024, kLayoutSw128);
+}
+__device__ __forceinline__ uint64_t desc_mnmajor(uint32_t saddr) {
+  return make_desc(saddr, 4096, 512, kLayoutSw128Atom32);
 }
 
 // Instruction descriptor: D f32, A/B tf32, A K-major or MN-major, B MN-major.
@@ -317,10 +332,10 @@ gemm3x_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ C
           // (1024 B) in the MN-major layout.
           const uint32_t aoff = TRANS_A ? kk * 1024 : kk * 32;
           const uint32_t boff = kk * 1024;
-          const uint64_t dah = TRANS_A ? make_desc(a_hi + aoff, 4096, 1024) : make_desc(a_hi + aoff, 16, 1024);
-          const uint64_t dal = TRANS_A ? make_desc(a_lo + aoff, 4096, 1024) : make_desc(a_lo + aoff, 16, 1024);
-          const uint64_t dbh = make_desc(b_hi + boff, 4096, 1024);
-          const uint64_t dbl = make_desc(b_lo + boff, 4096, 1024);
+          const uint64_t dah = TRANS_A ? desc_mnmajor(a_hi + aoff) : desc_kmajor(a_hi + aoff);
+          const uint64_t dal = TRANS_A ? desc_mnmajor(a_lo + aoff) : desc_kmajor(a_lo + aoff);
+          const uint64_t dbh = desc_mnmajor(b_hi + boff);
+          const uint64_t dbl = desc_mnmajor(b_lo + boff);
           mma_tf32(tmem, dal, dbh, idesc, (it > 0 || kk > 0) ? 1u : 0u);
           mma_tf32(tmem, dah, dbl, idesc, 1u);
           mma_tf32(tmem, dah, dbh, idesc, 1u);
@@ -446,9 +461,11 @@ EncodeFn encode_fn() {
   return fn;
 }
 
-// 3-D fp32 tensor map {inner, outer, batch}, box {32, box_outer, 1}, 128B swizzle.
+// 3-D fp32 tensor map {inner, outer, batch}, box {32, box_outer, 1}.  K-major
+// operands use the 128B swizzle (16-byte atoms), MN-major operands the 128B
+// swizzle with 32-byte atoms, which is the layout TF32 UMMA reads MN-major.
 int make_map(CUtensorMap* tm, const float* base, int64_t inner, int64_t outer, int64_t batch,
-             int64_t row_stride_elems, int64_t batch_stride_elems, int box_outer) {
+             int64_t row_stride_elems, int64_t batch_stride_elems, int box_outer, bool mn_major) {
   EncodeFn enc = encode_fn();
   KB_REQUIRE(enc != nullptr, KB_ERR_CUDA, "cuTensorMapEncodeTiled unavailable");
   cuuint64_t dims[3] = {(cuuint64_t)inner, (cuuint64_t)outer, (cuuint64_t)batch};
@@ -456,7 +473,8 @@ int make_map(CUtensorMap* tm, const float* base, int64_t inner, int64_t outer, i
   cuuint32_t box[3] = {32, (cuuint32_t)box_outer, 1};
   cuuint32_t estr[3] = {1, 1, 1};
   CUresult r = enc(tm, CU_TENSOR_MAP_DATA_TYPE_FLOAT32, 3, const_cast<float*>(base), dims, strides, box, estr,
-                   CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B,
+                   CU_TENSOR_MAP_INTERLEAVE_NONE,
+                   mn_major ? CU_TENSOR_MAP_SWIZZLE_128B_ATOM_32B : CU_TENSOR_MAP_SWIZZLE_128B,
                    CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
   KB_REQUIRE(r == CUDA_SUCCESS, KB_ERR_CUDA, "cuTensorMapEncodeTiled failed (%d)", (int)r);
   return KB_OK;
@@ -507,11 +525,11 @@ int run_gemm(const GemmArgs& g, int splits, float* ws, cudaStream_t s) {
   const int BN = bn256 ? 256 : 128;
   CUtensorMap ta, tb;
   if (g.trans_a) {
-    if (int st = make_map(&ta, g.A, g.M, g.K, g.batch, g.lda, g.sA, 32)) return st;
+    if (int st = make_map(&ta, g.A, g.M, g.K, g.batch, g.lda, g.sA, 32, true)) return st;
   } else {
-    if (int st = make_map(&ta, g.A, g.K, g.M, g.batch, g.lda, g.sA, BM)) return st;
+    if (int st = make_map(&ta, g.A, g.K, g.M, g.batch, g.lda, g.sA, BM, false)) return st;
   }
-  if (int st = make_map(&tb, g.B, g.N, g.K, g.batch, g.ldb, g.sB, 32)) return st;
+  if (int st = make_map(&tb, g.B, g.N, g.K, g.batch, g.ldb, g.sB, 32, true)) return st;
   const int nk = (int)ceil_div(g.K, BK);
   Params p{};
   p.M = (int)g.M;

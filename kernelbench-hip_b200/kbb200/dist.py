@@ -1,0 +1,111 @@
+"""Multi-GPU sharding of the operator library (one process per GPU).
+
+Ops whose units are independent (elementwise, row ops, dim-1 reductions,
+max-pool, GEMM rows, GEMV rows) shard by rows or batch items and need no
+collective: each rank runs the single-GPU kernel on its shard.  Four ops have a
+real exchange step, and each takes exactly one collective between a local
+partial kernel and a local finishing kernel (the split C-ABI entry pairs):
+
+    op                 local partial            collective            finish
+    mse_loss           sum (a-b)^2  (fp64)      all_reduce 8 B        divide by total count
+    frobenius          sum x^2      (fp64)      all_reduce 8 B        x / sqrt(total)
+    batch_norm_train   per-channel sum, sum^2   all_reduce 16*C B     normalise + affine
+    matmul_splitk      partial C over K slice   all_reduce M*N*4 B    (result replicated)
+
+Collectives go through torch.distributed (NCCL over NVLink on B200s).  The
+per-shard kernels are injectable (`kernels=`) so the composition can be
+tested with CPU implementations on a gloo process group; by default they are
+the CUDA kernels of kbb200.ops.
+"""
+from __future__ import annotations
+
+import math
+
+import torch
+import torch.distributed as tdist
+
+
+def _default_kernels():
+    from . import ops
+
+    return ops
+
+
+def _world(group=None) -> tuple[int, int]:
+    if not tdist.is_available() or not tdist.is_initialized():
+        return 0, 1
+    return tdist.get_rank(group), tdist.get_world_size(group)
+
+
+def shard_range(n: int, rank: int, world: int) -> tuple[int, int]:
+    """[lo, hi) of rank's contiguous share of n units (first n % world ranks
+    take one extra unit)."""
+    base, extra = divmod(n, world)
+    lo = rank * base + min(rank, extra)
+    return lo, lo + base + (1 if rank < extra else 0)
+
+
+def shard(t: torch.Tensor, rank: int, world: int, dim: int = 0) -> torch.Tensor:
+    lo, hi = shard_range(t.shape[dim], rank, world)
+    return t.narrow(dim, lo, hi - lo)
+
+
+def _all_reduce_sum(t: torch.Tensor, group=None) -> torch.Tensor:
+    if _world(group)[1] > 1:
+        tdist.all_reduce(t, op=tdist.ReduceOp.SUM, group=group)
+    return t
+
+
+def global_count(local: int, device, group=None) -> int:
+    """Sum of a per-rank element count (one small all_reduce)."""
+    if _world(group)[1] == 1:
+        return int(local)
+    c = torch.tensor([float(local)], dtype=torch.float64, device=device)
+    _all_reduce_sum(c, group)
+    return int(c.item())
+
+
+def mse_loss(a: torch.Tensor, b: torch.Tensor, total_n: int | None = None, out=None, group=None,
+             kernels=None):
+    """mean((a - b)^2) over the union of all ranks' shards (replicated 0-d
+    result).  total_n defaults to world_size * a.numel() (equal shards)."""
+    k = kernels or _default_kernels()
+    _, world = _world(group)
+    part = k.mse_partial(a, b)
+    _all_reduce_sum(part, group)
+    n = total_n if total_n is not None else a.numel() * world
+    return k.mse_finalize(part, n, out=out)
+
+
+def frobenius_normalize(x: torch.Tensor, out=None, group=None, kernels=None):
+    """x_shard / ||x||_F where the norm spans all ranks' shards."""
+    k = kernels or _default_kernels()
+    part = k.sumsq_partial(x)
+    _all_reduce_sum(part, group)
+    return k.scale_by_inv_norm(x, part, out=out)
+
+
+def batch_norm_train(x: torch.Tensor, weight=None, bias=None, eps: float = 1e-5,
+                     momentum: float = 0.1, running_mean=None, running_var=None, out=None,
+                     total_count: int | None = None, group=None, kernels=None):
+    """Training-mode BatchNorm with statistics over the global batch (every
+    rank holds a slice of the batch dim): SyncBatchNorm semantics, equal to
+    BatchNorm on the concatenated batch."""
+    k = kernels or _default_kernels()
+    _, world = _world(group)
+    stats = k.batch_norm_stats(x)
+    _all_reduce_sum(stats, group)
+    per_rank = x.shape[0] * math.prod(x.shape[2:])
+    count = total_count if total_count is not None else per_rank * world
+    return k.batch_norm_apply(x, stats, count, weight, bias, eps, momentum, running_mean,
+                              running_var, out=out)
+
+
+def matmul_splitk(a: torch.Tensor, b: torch.Tensor, out=None, group=None, kernels=None):
+    """C = A @ B with K sharded: rank r holds A[:, K_r] and B[K_r, :].  Each
+    rank computes its partial C (split-K across its own SMs as well), then one
+    all_reduce sums the partials; every rank ends with the full C."""
+    k = kernels or _default_kernels()
+    c = k.matmul_splitk(a, b, out=out)
+    _all_reduce_sum(c, group)
+    return c

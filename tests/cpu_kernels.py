@@ -1,0 +1,65 @@
+"""CPU stand-ins for the per-shard CUDA kernels used by kbb200.dist, so the
+sharding and collective composition can run on gloo ranks without a GPU.
+They follow the C-ABI contracts: fp64 partials, fp32 outputs."""
+from __future__ import annotations
+
+import torch
+
+
+def mse_partial(a, b):
+    d = a.double() - b.double()
+    return (d * d).sum().reshape(())
+
+
+def mse_finalize(total, total_n, out=None):
+    r = (total / total_n).float()
+    if out is not None:
+        out.copy_(r)
+        return out
+    return r
+
+
+def sumsq_partial(x):
+    return (x.double() ** 2).sum().reshape(())
+
+
+def scale_by_inv_norm(x, total, out=None):
+    norm = torch.sqrt(total).float()
+    r = x / norm
+    if out is not None:
+        out.copy_(r)
+        return out
+    return r
+
+
+def batch_norm_stats(x):
+    axes = [0] + list(range(2, x.dim()))
+    xd = x.double()
+    return torch.stack([xd.sum(axes), (xd * xd).sum(axes)])
+
+
+def batch_norm_apply(x, stats, count, weight, bias, eps, momentum, running_mean, running_var, out=None):
+    mean = stats[0] / count
+    var = (stats[1] / count - mean * mean).clamp_min(0)
+    shape = [1, -1] + [1] * (x.dim() - 2)
+    y = (x.double() - mean.reshape(shape)) / torch.sqrt(var + eps).reshape(shape)
+    if weight is not None:
+        y = y * weight.double().reshape(shape)
+    if bias is not None:
+        y = y + bias.double().reshape(shape)
+    if running_mean is not None:
+        running_mean.mul_(1 - momentum).add_(momentum * mean.float())
+        running_var.mul_(1 - momentum).add_(momentum * (var * count / max(count - 1, 1)).float())
+    y = y.float()
+    if out is not None:
+        out.copy_(y)
+        return out
+    return y
+
+
+def matmul_splitk(a, b, out=None):
+    r = (a.double() @ b.double()).float()
+    if out is not None:
+        out.copy_(r)
+        return out
+    return r
