@@ -205,34 +205,27 @@ def make_runner(name: str, inputs: list, world: int, rank: int):
     raise KeyError(name)
 
 
-def e2e_runner(name: str, host_inputs: list, host_out: torch.Tensor, device):
+def load_candidate(problem: str):
+    """The candidate module for `problem` (ENTRY + Model), the public API."""
+    import importlib.util
+
+    path = REPO / "kernelbench-hip_b200" / "candidates" / problem / "b200.py"
+    spec = importlib.util.spec_from_file_location(f"cand_{problem}", path)
+    mod = importlib.util.module_from_spec(spec)
+    spec.loader.exec_module(mod)
+    return mod
+
+
+def e2e_runner(problem: str, host_inputs: list, host_out: torch.Tensor, device):
     """One end-to-end call through the candidate API: pinned host inputs ->
-    device, Model.forward (the EXT entry), result -> pinned host."""
-    import kbb200.ext as EXT
+    device, Model.forward (the compiled EXT entry), result -> pinned host."""
+    model = load_candidate(problem).Model().to(device)
 
     def run():
         d = [h.to(device, non_blocking=True) for h in host_inputs]
-        out = torch.empty(host_out.shape, device=device, dtype=host_out.dtype)
-        if name == "layer_norm":
-            EXT.layernorm_entry(d[0], out, d[1], d[2], 1e-5)
-        elif name == "rms_norm":
-            F = d[0].shape[-1]
-            EXT.rmsnorm_entry(d[0], out, d[1], 1e-5, d[0].numel() // F, F, 1)
-        elif name == "softmax":
-            EXT.softmax_entry(d[0], out)
-        elif name == "log_softmax":
-            EXT.logsoftmax_entry(d[0], out)
-        elif name == "gelu_tanh":
-            EXT.mingpt_gelu_entry(d[0], out)
-        elif name == "gelu_erf":
-            EXT.gelu_entry(d[0], out)
-        elif name == "swish":
-            EXT.swish_entry(d[0], out)
-        elif name == "relu":
-            EXT.relu_entry(d[0], out)
-        else:
-            raise KeyError(f"e2e not wired for {name}")
-        host_out.copy_(out, non_blocking=True)
+        with torch.no_grad():
+            out = model(*d)
+        host_out.copy_(out.reshape(host_out.shape), non_blocking=True)
 
     return run
 
@@ -289,6 +282,35 @@ def cpu_reference(ops: list[str], steps: int, warmup: int, threads: int,
             "seconds": round(dt, 3), "steps": steps}
 
 
+# ----------------------------------------------------------------- profiling driver
+def profile_op(op: str, frac: float, reps: int = 3) -> int:
+    """Run one op `reps` times on a reduced copy of its benchmark input (the
+    leading dim scaled by `frac`; GEMMs at 4096^3 or a K/batch fraction) so a
+    single launch can be captured by ncu within a few GB of device memory."""
+    from kbb200 import ops as K
+    from kbb200.workloads import WORKLOADS, make_inputs
+
+    w = WORKLOADS[op]
+    dev = torch.device("cuda:0")
+    shapes = {}
+    for nm, shape, _ in w.inputs:
+        if op == "matmul":
+            shapes[nm] = (4096, 4096)
+        elif op == "matmul_splitk":
+            shapes[nm] = (shape[0], int(shape[1] * frac)) if nm == "A" else (int(shape[0] * frac), shape[1])
+        elif nm in ("x", "predictions", "targets", "A", "B") and len(shape) > 1 or nm in ("predictions", "targets"):
+            if op == "gemv" and nm == "x":
+                continue
+            shapes[nm] = (max(1, int(shape[0] * frac)),) + tuple(shape[1:])
+    ins = make_inputs(w, dev, 0, shapes)
+    runner, _ = make_runner(op, ins, 1, 0)
+    for _ in range(reps):
+        runner()
+    torch.cuda.synchronize()
+    print("profiled", op, [tuple(t.shape) for t in ins], flush=True)
+    return 0
+
+
 # ----------------------------------------------------------------- main
 def main() -> int:
     ap = argparse.ArgumentParser()
@@ -300,7 +322,11 @@ def main() -> int:
     ap.add_argument("--no-e2e", action="store_true")
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--cpu-steps", type=int, default=3)
+    ap.add_argument("--profile-op", default=None, help="run one op 3x on a reduced input (for ncu)")
+    ap.add_argument("--frac", type=float, default=0.25, help="input fraction for --profile-op")
     a = ap.parse_args()
+    if a.profile_op:
+        return profile_op(a.profile_op, a.frac)
     if a.warmup < 3 and a.impl == "ours":
         a.warmup = 3
 
@@ -424,7 +450,7 @@ def main() -> int:
         for n, w, ins, _, out in runners:
             hin = [t.cpu().pin_memory() for t in ins]
             hout = torch.empty(out.shape, dtype=out.dtype).pin_memory()
-            e2e_fns.append(e2e_runner(n, hin, hout, device))
+            e2e_fns.append(e2e_runner(w.problem, hin, hout, device))
             h2d += bytes_of(hin)
             d2h += bytes_of([hout])
         for f in e2e_fns:

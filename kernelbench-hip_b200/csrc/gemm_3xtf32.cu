@@ -2,12 +2,15 @@
 // with the 3xTF32 split, for square, batched and split-K shapes.
 //
 // fp32 accuracy from TF32 tensor cores: every operand element x is split into
-// hi = rna_tf32(x) (TF32 keeps 10 explicit mantissa bits) and lo = x - hi
-// (exact in fp32), and the product is accumulated in fp32 as
+// hi = x with its low 13 mantissa bits cleared (TF32 keeps 10 explicit bits;
+// truncation toward zero) and lo = x - hi (exact in fp32, same sign as x),
+// and the product is accumulated in fp32 as
 //     C += A_lo * B_hi + A_hi * B_lo + A_hi * B_hi
 // (the A_lo * B_lo term is below fp32 resolution).  Because hi has its low 13
 // bits cleared, the result does not depend on whether the tensor core rounds
-// or truncates its fp32 inputs to TF32.
+// or truncates its fp32 inputs to TF32; because hi and lo share the sign of
+// x, an infinite operand meets b_hi and b_lo of one sign and yields +-inf as
+// in plain fp32, not inf - inf.  Non-finite x keeps hi = x, lo = 0.
 //
 // Kernel structure (one CTA per 128 x BN output tile, 192 threads):
 //   warp 0      TMA producer: cp.async.bulk.tensor loads of the A tile
@@ -166,10 +169,8 @@ __device__ __forceinline__ void tmem_ld32(uint32_t taddr, uint32_t (&r)[32]) {
 __device__ __forceinline__ void tmem_ld_wait() {
   asm volatile("tcgen05.wait::ld.sync.aligned;" ::: "memory");
 }
-__device__ __forceinline__ float tf32_rna(float x) {
-  uint32_t r;
-  asm("cvt.rna.tf32.f32 %0, %1;" : "=r"(r) : "f"(x));
-  return __uint_as_float(r);
+__device__ __forceinline__ float tf32_trunc(float x) {
+  return __uint_as_float(__float_as_uint(x) & 0xFFFFE000u);
 }
 
 // UMMA shared-memory descriptors (version 1).  TF32 operands come in two
@@ -212,7 +213,7 @@ __device__ __forceinline__ void split_buffer(float4* buf, float4* lo, int n4, in
 #pragma unroll 4
   for (int i = t; i < n4; i += kConvThreads) {
     float4 v = buf[i], h, l;
-    h.x = tf32_rna(v.x); h.y = tf32_rna(v.y); h.z = tf32_rna(v.z); h.w = tf32_rna(v.w);
+    h.x = tf32_trunc(v.x); h.y = tf32_trunc(v.y); h.z = tf32_trunc(v.z); h.w = tf32_trunc(v.w);
     l.x = v.x - h.x; l.y = v.y - h.y; l.z = v.z - h.z; l.w = v.w - h.w;
     if (!isfinite(l.x)) { h.x = v.x; l.x = 0.f; }
     if (!isfinite(l.y)) { h.y = v.y; l.y = 0.f; }

@@ -79,7 +79,7 @@ def assert_close(got, want, tol, what: str = "") -> None:
     w = want.astype(np.float64)
     nan_ok = np.isnan(g) == np.isnan(w)
     assert nan_ok.all(), f"{what}: NaN pattern differs"
-    m = ~np.isnan(w)
+    m = ~np.isnan(w) & ~(np.isinf(w) & (g == w))   # equal infinities match
     err = np.abs(g[m] - w[m])
     lim = tol + tol * np.abs(w[m])
     if not (err <= lim).all():

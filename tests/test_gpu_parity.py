@@ -393,3 +393,24 @@ def test_gemm_full_size_vs_torch_fp32(name, cuda_device):
     assert torch.isclose(got, want, atol=1e-3, rtol=1e-3).all()
     del A, B, got, want
     torch.cuda.empty_cache()
+
+
+@pytest.mark.parametrize("mnk", [(1024, 1024, 4096), (512, 768, 8192)])
+def test_gemm_accuracy_matches_fp32_cublas(mnk, cuda_device):
+    """3xTF32 error against an fp64 reference stays at fp32 level: within 4x
+    the error of torch's plain fp32 (non-TF32) matmul on the same data."""
+    from kbb200 import ops as K
+
+    M, N, Kd = mnk
+    g = torch.Generator(device=cuda_device).manual_seed(11)
+    A = torch.randn(M, Kd, device=cuda_device, generator=g)
+    B = torch.randn(Kd, N, device=cuda_device, generator=g)
+    ref = A.double() @ B.double()
+    prev = torch.backends.cuda.matmul.allow_tf32
+    torch.backends.cuda.matmul.allow_tf32 = False
+    try:
+        e_torch = ((A @ B).double() - ref).abs().max().item()
+    finally:
+        torch.backends.cuda.matmul.allow_tf32 = prev
+    e_ours = (K.matmul(A, B).double() - ref).abs().max().item()
+    assert e_ours <= 4 * e_torch + 1e-6, f"3xTF32 max error {e_ours:.3e} vs fp32 {e_torch:.3e}"
