@@ -47,9 +47,19 @@ LAUNCHES = {"gelu_tanh": 1, "gelu_erf": 1, "swish": 1, "relu": 1, "layer_norm": 
             "mse_loss": 2, "frobenius_normalize": 2, "max_pool2d": 1, "batch_norm_train": 2,
             "matmul": 1, "bmm": 1, "matmul_splitk": 2, "gemv": 1}
 
-# DRAM bytes per launch (dram__bytes_read.sum + dram__bytes_write.sum) from the
-# committed ncu summaries in profiles/; None until captured.
-NCU_DRAM_BYTES: dict[str, float | None] = {}
+# DRAM bytes per full-size launch (dram__bytes_read.sum + dram__bytes_write.sum)
+# from the ncu captures summarised in profiles/: captured on a quarter of the
+# rows (or the full tensor for gelu) and scaled by the rows processed, which
+# the streaming kernels' traffic is proportional to.
+NCU_DRAM_BYTES: dict[str, float | None] = {
+    "layer_norm": 4.0 * (536.950528e6 + 483.113216e6),
+    "softmax": 4.0 * (268.451072e6 + 216.415232e6),
+    "gelu_tanh": 268.449024e6 + 221.055488e6,
+    "sum_dim": 4.0 * (2147.519e6 + 3.969536e6),
+    "max_pool2d": 4.0 * (554.001664e6 + 81.265152e6),
+    "gemv": 4.0 * (4299.428e6 + 3.49568e6),
+    "batch_norm_train": 4.0 * (536.913408e6 + 4.80512e6 + 536.905984e6 + 490.593024e6),
+}
 
 # bounded CPU samples (fraction of the leading dim) for the CPU reference arm
 CPU_SAMPLE_ROWS = {"layer_norm": 1024, "rms_norm": 1024, "softmax": 256, "log_softmax": 256,

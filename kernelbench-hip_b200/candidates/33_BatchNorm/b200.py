@@ -15,7 +15,7 @@ class Model(torch.nn.Module):
         self.register_buffer("running_mean", torch.zeros(num_features))
         self.register_buffer("running_var", torch.ones(num_features))
 
-    def forward(self, x, weight, bias):
+    def forward(self, x, weight=None, bias=None):
         y = torch.empty_like(x)
         EXT.bn_entry(x, y, weight, bias, self.eps, self.momentum, self.running_mean,
                      self.running_var)

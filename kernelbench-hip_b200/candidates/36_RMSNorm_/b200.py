@@ -9,15 +9,24 @@ import kbb200.ext as EXT
 
 
 class Model(torch.nn.Module):
-    def __init__(self, eps: float = 1e-5):
+    """RMSNorm.  Given `num_features` (the reference's constructor), x is
+    [B, num_features, ...] normalised over dim 1; otherwise over the last dim,
+    with an optional per-feature weight."""
+
+    def __init__(self, num_features: int | None = None, eps: float = 1e-5):
         super().__init__()
+        self.num_features = num_features
         self.eps = eps
 
-    def forward(self, x, weight):
+    def forward(self, x, weight=None):
         y = torch.empty_like(x)
-        F = x.size(-1)
-        rows = x.numel() // F
-        EXT.rmsnorm_entry(x, y, weight, self.eps, rows, F, 1)
+        if self.num_features is not None and x.dim() > 2:
+            F = x.size(1)
+            inner = x[0, 0].numel()
+            EXT.rmsnorm_entry(x, y, weight, self.eps, x.size(0) * inner, F, inner)
+        else:
+            F = x.size(-1)
+            EXT.rmsnorm_entry(x, y, weight, self.eps, x.numel() // F, F, 1)
         return y
 
 

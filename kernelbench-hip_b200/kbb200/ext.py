@@ -44,11 +44,12 @@ def logsoftmax_entry(x: torch.Tensor, y: torch.Tensor) -> None:
     ops.log_softmax(x, out=y)
 
 
-def layernorm_entry(x, y, weight, bias, eps: float) -> None:
+def layernorm_entry(x, y, weight, bias, eps: float, normalized_size: int | None = None) -> None:
     """candidates/40_LayerNorm/v1.py:62 — (x, y, mean, var, eps) there; the two
     scratch slots carry weight and bias here (None = identity affine).  The
-    normalized size is weight.numel(), else the last dim."""
-    ops.layer_norm(x, weight, bias, eps, out=y)
+    normalized size is `normalized_size`, else weight.numel(), else the last
+    dim."""
+    ops.layer_norm(x, weight, bias, eps, normalized_size=normalized_size, out=y)
 
 
 def rmsnorm_entry(x, y, weight, eps: float, rows: int, F: int, inner: int) -> None:

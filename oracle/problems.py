@@ -158,11 +158,11 @@ PROBLEMS: dict[str, tuple] = {
     "26_GELU_": (GeluErf, [], (("x", _N_EW, "normal"),), {"x": (37, 301)}),
     "25_Swish": (Swish, [], (("x", _N_EW, "normal"),), {"x": (37, 301)}),
     "19_ReLU": (Relu, [], (("x", _N_EW, "normal"),), {"x": (37, 301)}),
-    "40_LayerNorm": (LayerNormLast, [1e-5],
+    "40_LayerNorm": (LayerNormLast, [],
                      (("x", (65536, 8192), "normal"), ("weight", (8192,), "gamma"),
                       ("bias", (8192,), "beta")),
                      {"x": (33, 8192), "weight": (8192,), "bias": (8192,)}),
-    "36_RMSNorm_": (RmsNormLast, [1e-5],
+    "36_RMSNorm_": (RmsNormLast, [],
                     (("x", (65536, 8192), "normal"), ("weight", (8192,), "gamma")),
                     {"x": (33, 8192), "weight": (8192,)}),
     "23_Softmax": (Softmax, [], (("x", (8192, 32768), "normal_std2"),), {"x": (5, 32768)}),
