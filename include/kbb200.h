@@ -154,6 +154,25 @@ KB_API int kb_batchnorm_train_f32(const float* x, const float* gamma,
                            float* running_mean, float* running_var,
                            void* workspace, size_t workspace_bytes,
                            kbStream stream);
+/* Allocation-free training-mode BatchNorm: no counterpart in the reference.
+ * Same arguments and results as kb_batchnorm_train_f32 minus the workspace,
+ * for callers that may not allocate device memory themselves: libraries
+ * running inside a host framework that owns every device allocation through
+ * its own pool or budget, and latency-bound loops where cudaMalloc's implicit
+ * device synchronisation is not acceptable.  The per-channel partial sums
+ * live in a 128 KiB file-scope device array (8192 fp64 pairs) that every
+ * device loading the library keeps until process exit, so C * splits must be
+ * <= 8192, where splits = max(1, min(N, ceil(4 * SMs / C))), so any
+ * C <= 8192 fits on a 148-SM B200.  Larger C returns KB_ERR_UNSUPPORTED.  The first
+ * call on a device looks up the array's device address
+ * (cudaGetSymbolAddress); make it before any stream capture.  Every call
+ * shares the one array, so calls that overlap on the GPU (for example on two
+ * streams) race; the caller must serialise them.  Calls no cudaMalloc.     */
+KB_API int kb_batchnorm_train_f32_noalloc(const float* x, const float* gamma,
+                                          const float* beta, float* y, int64_t N,
+                                          int64_t C, int64_t HW, float eps,
+                                          float momentum, float* running_mean,
+                                          float* running_var, kbStream stream);
 /* sharded form: stats[0:C] = per-channel sum, stats[C:2C] = per-channel sum
  * of squares over this shard (fp64); a collective adds them across shards,
  * then kb_batchnorm_apply_f32 normalises with `total_count` elements per

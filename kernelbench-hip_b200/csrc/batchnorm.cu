@@ -10,6 +10,8 @@
 // derives mean / inv-std in fp64 and writes y = (x - mean) * (inv_std * gamma)
 // + beta.  x is read twice (2 GiB does not fit on chip); planes are applied in
 // reverse order so the first ones still sit in L2 from the end of pass 1.
+#include <mutex>
+
 #include "kb_common.cuh"
 
 namespace kb {
@@ -154,6 +156,37 @@ bn_apply_kernel(const float* __restrict__ x, const float* __restrict__ gamma,
     yp[i] = (xp[i] - mean) * scale + shift;
 }
 
+// ---------------------------------------------------------------------------
+// Allocation-free variant: the per-channel partials live in this file-scope
+// device array instead of caller workspace.  Every device that loads the
+// library holds it until exit.  Host code must not pass the symbol itself to a
+// kernel (on the host it is only a stand-in, not a device address); the
+// device address is looked up once per device with cudaGetSymbolAddress.
+// ---------------------------------------------------------------------------
+constexpr int kNoAllocPartials = 8192;  // (sum, sum of squares) pairs: 128 KiB
+static __device__ __align__(256) double2 g_bn_noalloc_partials[kNoAllocPartials];
+
+std::mutex g_noalloc_mu;
+double2* g_noalloc_ptr[64] = {};
+
+// Device address of g_bn_noalloc_partials on the current device; the first
+// call on a device performs the lookup.
+int noalloc_partials(double2** out) {
+  int dev = 0;
+  KB_CUDA(cudaGetDevice(&dev));
+  KB_REQUIRE(dev >= 0 && dev < 64, KB_ERR_DEVICE, "device ordinal %d out of range", dev);
+  std::lock_guard<std::mutex> lock(g_noalloc_mu);
+  if (g_noalloc_ptr[dev] == nullptr) {
+    void* p = nullptr;
+    const cudaError_t e = cudaGetSymbolAddress(&p, g_bn_noalloc_partials);
+    if (e != cudaSuccess || p == nullptr)
+      return set_error(KB_ERR_CUDA, "cudaGetSymbolAddress(batchnorm scratch): %s", cudaGetErrorString(e));
+    g_noalloc_ptr[dev] = static_cast<double2*>(p);
+  }
+  *out = g_noalloc_ptr[dev];
+  return KB_OK;
+}
+
 int bn_check(const char* name, const float* x, int64_t N, int64_t C, int64_t HW) {
   KB_REQUIRE(N >= 0 && C >= 0 && HW >= 0, KB_ERR_INVALID_ARG, "%s: negative size", name);
   KB_REQUIRE(x || N * C * HW == 0, KB_ERR_INVALID_ARG, "%s: null input", name);
@@ -189,6 +222,30 @@ int kb_batchnorm_train_f32(const float* x, const float* gamma, const float* beta
   const bool vec = HW % 4 == 0 && kb::aligned16(x) && kb::aligned16(y);
   double2* parts = static_cast<double2*>(workspace);
   kb::BnShape sh{N, C, HW};
+  kb::bn_stats_kernel<<<dim3((unsigned)C, (unsigned)S), kb::kThreads, 0, stream>>>(x, sh, S, vec, parts);
+  if (int st = kb::check_launch(name)) return st;
+  kb::bn_apply_kernel<<<(unsigned)(N * C), kb::kThreads, 0, stream>>>(
+      x, gamma, beta, y, sh, parts, S, nullptr, N * HW, eps, momentum, running_mean, running_var, vec);
+  return kb::check_launch(name);
+}
+
+int kb_batchnorm_train_f32_noalloc(const float* x, const float* gamma, const float* beta, float* y,
+                                   int64_t N, int64_t C, int64_t HW, float eps, float momentum,
+                                   float* running_mean, float* running_var, kbStream stream) {
+  const char* name = "kb_batchnorm_train_f32_noalloc";
+  if (int st = kb::bn_check(name, x, N, C, HW)) return st;
+  if (N * C * HW == 0) return KB_OK;
+  KB_REQUIRE(y, KB_ERR_INVALID_ARG, "%s: null output", name);
+  const int S = kb::bn_splits(N, C);
+  KB_REQUIRE(C * S <= kb::kNoAllocPartials, KB_ERR_UNSUPPORTED,
+             "%s: %lld channels x %d batch splits need %lld partial slots; the built-in scratch "
+             "holds %d (use kb_batchnorm_train_f32 with caller workspace)",
+             name, (long long)C, S, (long long)(C * S), kb::kNoAllocPartials);
+  double2* parts = nullptr;
+  if (int st = kb::noalloc_partials(&parts)) return st;
+  const bool vec = HW % 4 == 0 && kb::aligned16(x) && kb::aligned16(y);
+  kb::BnShape sh{N, C, HW};
+  // every used slot is overwritten by the stats kernel: nothing to clear
   kb::bn_stats_kernel<<<dim3((unsigned)C, (unsigned)S), kb::kThreads, 0, stream>>>(x, sh, S, vec, parts);
   if (int st = kb::check_launch(name)) return st;
   kb::bn_apply_kernel<<<(unsigned)(N * C), kb::kThreads, 0, stream>>>(

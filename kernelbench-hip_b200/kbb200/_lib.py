@@ -49,6 +49,7 @@ SIGNATURES: dict[str, tuple] = {
     "kb_maxpool2d_f32": (_int, [_p, _p, _i64, _i64, _i64, _i64, _i64, _i64, _int, _int, _int, _int, _p]),
     "kb_batchnorm_workspace_size": (_sz, [_i64, _i64, _i64]),
     "kb_batchnorm_train_f32": (_int, [_p, _p, _p, _p, _i64, _i64, _i64, _float, _float, _p, _p, _p, _sz, _p]),
+    "kb_batchnorm_train_f32_noalloc": (_int, [_p, _p, _p, _p, _i64, _i64, _i64, _float, _float, _p, _p, _p]),
     "kb_batchnorm_stats_f64": (_int, [_p, _p, _i64, _i64, _i64, _p, _sz, _p]),
     "kb_batchnorm_apply_f32": (_int, [_p, _p, _p, _p, _p, _i64, _i64, _i64, _i64, _float, _float, _p, _p, _p]),
     "kb_sgemm_3xtf32": (_int, [_p, _p, _p, _i64, _i64, _i64, _i64, _i64, _i64, _int, _p]),
