@@ -1,32 +1,40 @@
 // gemm_3xtf32.cu — fp32 GEMM on the 5th-generation tensor cores (tcgen05)
 // with the 3xTF32 split, for square, batched and split-K shapes.
 //
-// fp32 accuracy from TF32 tensor cores: every operand element x is split into
-// hi = x with its low 13 mantissa bits cleared (TF32 keeps 10 explicit bits;
-// truncation toward zero) and lo = x - hi (exact in fp32, same sign as x),
-// and the product is accumulated in fp32 as
-//     C += A_lo * B_hi + A_hi * B_lo + A_hi * B_hi
-// (the A_lo * B_lo term is below fp32 resolution).  Because hi has its low 13
-// bits cleared, the result does not depend on whether the tensor core rounds
-// or truncates its fp32 inputs to TF32; because hi and lo share the sign of
-// x, an infinite operand meets b_hi and b_lo of one sign and yields +-inf as
-// in plain fp32, not inf - inf.  Non-finite x keeps hi = x, lo = 0.
+// fp32 accuracy from TF32 tensor cores.  Every operand element x is split as
+// hi = x with its low 13 mantissa bits cleared (TF32 keeps 10 explicit bits)
+// and lo = x - hi (exact in fp32, same sign as x), and
+//     C = sum over K of  A_lo * B_hi + A_hi * B_lo + A_hi * B_hi
+// (A_lo * B_lo is below fp32 resolution).  The tensor core itself truncates
+// an fp32 operand to TF32, i.e. reads x as hi (verified bitwise on the B200),
+// so the raw tiles serve as the hi operands and only the lo tiles are
+// written.  An infinite operand meets b_hi and b_lo of one sign and yields
+// +-inf as plain fp32 does; non-finite x gets lo = 0.
 //
-// Kernel structure (one CTA per 128 x BN output tile, 192 threads):
-//   warp 0      TMA producer: cp.async.bulk.tensor loads of the A tile
-//               (128 x 32, K-major, 128B swizzle) and of the B tile
-//               (32 x BN, N-major, 32-column boxes, 128B swizzle with
-//               32-byte atoms) into an S-stage ring,
-//               completion tracked by mbarrier transaction counts.
-//   warps 2-5   split converters: rewrite each landed stage in place as the
-//               hi part and write the lo part to the stage's lo buffers
-//               (element-wise, so the swizzled layout is preserved), then
-//               fence the generic->async proxy and arrive on conv[s].
-//   warp 1      allocates the TMEM accumulator (BN columns x 128 lanes) and
-//               one elected lane issues 12 tcgen05.mma.kind::tf32 (4 K-steps
-//               x 3 products) per stage; tcgen05.commit frees the stage.
-//   warps 2-5   epilogue: tcgen05.ld the accumulator lane quarter each warp
-//               owns and store fp32 C (or the split-K partial tile).
+// The tensor core's fp32 accumulation is not round-to-nearest: its error
+// grows with the number of MMAs chained into one accumulator.  So K is cut
+// into chunks of kChunkK; each chunk is accumulated in one of two TMEM
+// buffers (ping-pong), and eight promotion warps add every finished chunk
+// into fp32 register totals with ordinary round-to-nearest adds.  The
+// error then scales with the magnitude of one chunk, not of the whole sum,
+// and stays at the level of an fp32 CUDA-core GEMM.
+//
+// CTA = one 128 x BN output tile, 512 threads in 4 warpgroups:
+//   warp 0       TMA producer: cp.async.bulk.tensor loads of the A tile
+//                (128 x 16, K-major, 64B swizzle) and B tile (16 x BN,
+//                N-major, 32-column boxes, 128B swizzle with 32-byte atoms)
+//                into a 4-stage ring; mbarrier transaction counts.
+//   warp 1       allocates TMEM (2 x BN columns) and one lane issues
+//                6 tcgen05.mma.kind::tf32 per stage (2 K-steps x 3 products);
+//                tcgen05.commit frees the stage and publishes finished chunks.
+//   warps 2-7    lo converters: write A_lo, B_lo for each landed stage
+//                (element-wise, so the swizzled layout carries over), fence
+//                generic -> async proxy, arrive on conv[s].
+//   warps 8-15   promotion + epilogue: tcgen05.ld each finished chunk, add
+//                into 128-lane x BN fp32 register totals (each warp owns one
+//                TMEM lane quarter and half the columns), store C at the end.
+// setmaxnreg moves registers from warpgroups 0-1 (64 each) to the promotion
+// warpgroups (192 each); the sum equals the 512 x 128 the CTA launches with.
 // Every mbarrier wait is bounded (%globaltimer); on expiry the CTA raises a
 // shared abort flag and a device fault word, all roles leave their loops,
 // outstanding TMA loads are drained (bounded) and TMEM is freed.
@@ -44,19 +52,26 @@ __device__ int g_gemm_fault = 0;  // nonzero after a CTA gave up waiting
 namespace gemm {
 
 constexpr int BM = 128;
-constexpr int BK = 32;               // fp32 elements = one 128-byte swizzle row
-constexpr int kThreads = 192;
-constexpr int kConvThreads = 128;    // warps 2..5
+constexpr int BK = 16;                 // fp32 K per stage: one 64-byte K-major row
+constexpr int kStages = 4;
+constexpr int kChunkK = 128;           // K elements per TMEM accumulation chunk
+constexpr int kChunkBlocks = kChunkK / BK;
+constexpr int kThreads = 512;
+constexpr int kConvWarp0 = 2, kConvWarps = 6;
+constexpr int kConvThreads = kConvWarps * 32;
+constexpr int kPromoWarp0 = 8, kPromoWarps = 8;
+constexpr int kPromoThreads = kPromoWarps * 32;
 constexpr uint64_t kWaitLimitNs = 2000000000ull;
 
 template <int BN>
 struct Cfg {
-  static constexpr int S = (BN == 256) ? 2 : 3;
-  static constexpr int A_BYTES = BM * BK * 4;
-  static constexpr int B_BYTES = BN * BK * 4;
-  static constexpr int STAGE_BYTES = 2 * (A_BYTES + B_BYTES);   // hi + lo buffers
+  static constexpr int A_BYTES = BM * BK * 4;                  // 8 KB
+  static constexpr int B_BYTES = BN * BK * 4;                  // 16 KB (BN 256)
+  static constexpr int STAGE_BYTES = 2 * (A_BYTES + B_BYTES);  // raw + lo buffers
   static constexpr int BAR_BYTES = 256;
-  static constexpr int SMEM_BYTES = S * STAGE_BYTES + BAR_BYTES + 1024;  // + alignment slack
+  static constexpr int SMEM_BYTES = kStages * STAGE_BYTES + BAR_BYTES + 1024;  // + alignment slack
+  static constexpr int TMEM_COLS = 2 * BN;                     // two chunk accumulators
+  static constexpr int COLS_PER_WARP = BN / 2;                 // promotion warps split columns
 };
 
 // ------------------------------------------------------------------ PTX wrappers
@@ -169,21 +184,17 @@ __device__ __forceinline__ void tmem_ld32(uint32_t taddr, uint32_t (&r)[32]) {
 __device__ __forceinline__ void tmem_ld_wait() {
   asm volatile("tcgen05.wait::ld.sync.aligned;" ::: "memory");
 }
-__device__ __forceinline__ float tf32_trunc(float x) {
-  return __uint_as_float(__float_as_uint(x) & 0xFFFFE000u);
-}
-
 // UMMA shared-memory descriptors (version 1).  TF32 operands come in two
 // canonical layouts, matching how TMA writes them:
-//   K-major  (A as stored [M, K]): 128-byte swizzle with 16-byte atoms
-//            (layout type 2); 8-row groups of 128-byte rows, SBO = 1024 B,
-//            LBO unused.  A K step of 8 tf32 advances the start by 32 B.
+//   K-major  (A as stored [M, K]): 64-byte swizzle (layout type 4); 64-byte
+//            rows, 8-row groups 512 B apart (SBO), LBO unused.  The second
+//            K step of 8 tf32 starts 32 B into each row.
 //   MN-major (B [K, N], and A stored [K, M]): TF32 accepts only the 128-byte
-//            swizzle with 32-byte atoms (layout type 1): 4-row groups of
-//            128-byte rows, SBO = 512 B between groups, LBO = 4096 B between
-//            the 32-element column blocks (one TMA box each).  A K step of 8
-//            rows advances the start by 1024 B.
-constexpr uint32_t kLayoutSw128 = 2;
+//            swizzle with 32-byte atoms (layout type 1): 128-byte rows in
+//            4-row groups 512 B apart (SBO), 32-element column blocks 2048 B
+//            apart (LBO, one 16-row TMA box each).  A K step of 8 rows
+//            advances the start by 1024 B.
+constexpr uint32_t kLayoutSw64 = 4;
 constexpr uint32_t kLayoutSw128Atom32 = 1;
 __device__ __forceinline__ uint64_t make_desc(uint32_t saddr, uint32_t lbo, uint32_t sbo, uint32_t layout) {
   uint64_t d = 0;
@@ -195,10 +206,10 @@ __device__ __forceinline__ uint64_t make_desc(uint32_t saddr, uint32_t lbo, uint
   return d;
 }
 __device__ __forceinline__ uint64_t desc_kmajor(uint32_t saddr) {
-  return make_desc(saddr, 16, 1024, kLayoutSw128);
+  return make_desc(saddr, 16, 512, kLayoutSw64);
 }
 __device__ __forceinline__ uint64_t desc_mnmajor(uint32_t saddr) {
-  return make_desc(saddr, 4096, 512, kLayoutSw128Atom32);
+  return make_desc(saddr, 2048, 512, kLayoutSw128Atom32);
 }
 
 // Instruction descriptor: D f32, A/B tf32, A K-major or MN-major, B MN-major.
@@ -207,21 +218,26 @@ __host__ __device__ constexpr uint32_t make_idesc(int M, int N, bool a_mn) {
          ((uint32_t)(N >> 3) << 17) | ((uint32_t)(M >> 4) << 24);
 }
 
-// Split the float4s [begin, n4) (stride kConvThreads) of `buf` in place into
-// hi and write lo to `lo`.  Non-finite inputs keep hi = x, lo = 0.
-__device__ __forceinline__ void split_buffer(float4* buf, float4* lo, int n4, int t) {
+__device__ __forceinline__ float lo_part(float x) {
+  const float l = x - __uint_as_float(__float_as_uint(x) & 0xFFFFE000u);
+  return isfinite(l) ? l : 0.0f;
+}
+
+// lo[i] = x[i] - tf32_trunc(x[i]) for the float4s t, t + stride, ...
+__device__ __forceinline__ void lo_buffer(const float4* __restrict__ src, float4* __restrict__ dst, int n4,
+                                          int t) {
 #pragma unroll 4
   for (int i = t; i < n4; i += kConvThreads) {
-    float4 v = buf[i], h, l;
-    h.x = tf32_trunc(v.x); h.y = tf32_trunc(v.y); h.z = tf32_trunc(v.z); h.w = tf32_trunc(v.w);
-    l.x = v.x - h.x; l.y = v.y - h.y; l.z = v.z - h.z; l.w = v.w - h.w;
-    if (!isfinite(l.x)) { h.x = v.x; l.x = 0.f; }
-    if (!isfinite(l.y)) { h.y = v.y; l.y = 0.f; }
-    if (!isfinite(l.z)) { h.z = v.z; l.z = 0.f; }
-    if (!isfinite(l.w)) { h.w = v.w; l.w = 0.f; }
-    buf[i] = h;
-    lo[i] = l;
+    const float4 v = src[i];
+    dst[i] = make_float4(lo_part(v.x), lo_part(v.y), lo_part(v.z), lo_part(v.w));
   }
+}
+
+__device__ __forceinline__ void setmaxnreg_dec64() {
+  asm volatile("setmaxnreg.dec.sync.aligned.u32 64;" ::: "memory");
+}
+__device__ __forceinline__ void setmaxnreg_inc192() {
+  asm volatile("setmaxnreg.inc.sync.aligned.u32 192;" ::: "memory");
 }
 
 struct Params {
@@ -237,12 +253,12 @@ template <int BN, bool TRANS_A>
 __global__ void __launch_bounds__(kThreads, 1)
 gemm3x_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUtensorMap tmB, Params p) {
   using CF = Cfg<BN>;
-  constexpr int S = CF::S;
+  constexpr int S = kStages;
   extern __shared__ uint8_t smem_raw[];
   uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
   uint64_t* bars = reinterpret_cast<uint64_t*>(smem + S * CF::STAGE_BYTES);
-  // bars[0..S) full, [S..2S) conv, [2S..3S) empty, [3S] acc
-  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(bars + 3 * S + 1);
+  // bars: [0,S) full, [S,2S) conv, [2S,3S) empty, [3S,3S+2) chunk_full, [3S+2,3S+4) chunk_empty
+  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(bars + 3 * S + 4);
   volatile int* abort_flag = reinterpret_cast<volatile int*>(tmem_slot + 1);
 
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
@@ -256,11 +272,13 @@ gemm3x_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ C
     batch = 0;
   }
   const int nk = max(kb_end - kb_begin, 0);
+  const int nchunks = (nk + kChunkBlocks - 1) / kChunkBlocks;
 
   auto full = [&](int s) { return smem_u32(bars + s); };
   auto conv = [&](int s) { return smem_u32(bars + S + s); };
   auto empty = [&](int s) { return smem_u32(bars + 2 * S + s); };
-  const uint32_t acc_bar = smem_u32(bars + 3 * S);
+  auto chunk_full = [&](int b) { return smem_u32(bars + 3 * S + b); };
+  auto chunk_empty = [&](int b) { return smem_u32(bars + 3 * S + 2 + b); };
 
   if (threadIdx.x == 0) {
     for (int s = 0; s < S; ++s) {
@@ -268,12 +286,15 @@ gemm3x_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ C
       mbar_init(conv(s), kConvThreads);
       mbar_init(empty(s), 1);
     }
-    mbar_init(acc_bar, 1);
+    for (int b = 0; b < 2; ++b) {
+      mbar_init(chunk_full(b), 1);
+      mbar_init(chunk_empty(b), kPromoThreads);
+    }
     *abort_flag = 0;
     fence_barrier_init();
   }
   if (warp == 1) {
-    tmem_alloc(smem_u32(tmem_slot), BN);
+    tmem_alloc(smem_u32(tmem_slot), CF::TMEM_COLS);
     tmem_relinquish();
   }
   tc_fence_before();
@@ -283,87 +304,117 @@ gemm3x_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ C
 
   auto stage_ptr = [&](int s) { return smem + s * CF::STAGE_BYTES; };
 
-  if (warp == 0) {
-    // ---------------- TMA producer
-    if (lane == 0) {
-      int issued = 0;
+  if (warp < kPromoWarp0) {
+    setmaxnreg_dec64();
+    if (warp == 0) {
+      // ---------------- TMA producer
+      if (lane == 0) {
+        int issued = 0;
+        for (int it = 0; it < nk; ++it) {
+          const int s = it % S;
+          if (!mbar_wait(empty(s), ((it / S) & 1) ^ 1, abort_flag)) break;
+          uint8_t* st = stage_ptr(s);
+          const int k0 = (kb_begin + it) * BK;
+          mbar_expect_tx(full(s), CF::A_BYTES + CF::B_BYTES);
+          if (TRANS_A) {
+#pragma unroll
+            for (int j = 0; j < BM / 32; ++j)
+              tma_load_3d(smem_u32(st + j * 2048), &tmA, full(s), m0 + 32 * j, k0, batch);
+          } else {
+            tma_load_3d(smem_u32(st), &tmA, full(s), k0, m0, batch);
+          }
+#pragma unroll
+          for (int j = 0; j < BN / 32; ++j)
+            tma_load_3d(smem_u32(st + CF::A_BYTES + j * 2048), &tmB, full(s), n0 + 32 * j, k0, batch);
+          ++issued;
+        }
+        // drain: every issued load must land before the CTA may exit
+        for (int it = max(issued - S, 0); it < issued; ++it) {
+          const int s = it % S;
+          const uint64_t t0 = globaltimer();
+          while (!mbar_try_wait(full(s), (it / S) & 1)) {
+            if (globaltimer() - t0 > kWaitLimitNs) break;
+          }
+        }
+      }
+    } else if (warp == 1) {
+      // ---------------- MMA issuer
+      if (lane == 0) {
+        constexpr uint32_t idesc = make_idesc(BM, BN, TRANS_A);
+        bool alive = true;
+        for (int it = 0; it < nk && alive; ++it) {
+          const int s = it % S;
+          const int c = it / kChunkBlocks, b = c & 1;
+          const bool chunk_first = (it % kChunkBlocks) == 0;
+          const bool chunk_last = (it % kChunkBlocks) == kChunkBlocks - 1 || it == nk - 1;
+          if (chunk_first && !mbar_wait(chunk_empty(b), ((c >> 1) & 1) ^ 1, abort_flag)) break;
+          if (!mbar_wait(conv(s), (it / S) & 1, abort_flag)) break;
+          tc_fence_after();
+          uint8_t* st = stage_ptr(s);
+          const uint32_t a_hi = smem_u32(st);
+          const uint32_t b_hi = a_hi + CF::A_BYTES;
+          const uint32_t a_lo = b_hi + CF::B_BYTES;
+          const uint32_t b_lo = a_lo + CF::A_BYTES;
+          const uint32_t d = tmem + (uint32_t)(b * BN);
+#pragma unroll
+          for (int kk = 0; kk < BK / 8; ++kk) {
+            const uint32_t aoff = TRANS_A ? kk * 1024 : kk * 32;
+            const uint32_t boff = kk * 1024;
+            const uint64_t dah = TRANS_A ? desc_mnmajor(a_hi + aoff) : desc_kmajor(a_hi + aoff);
+            const uint64_t dal = TRANS_A ? desc_mnmajor(a_lo + aoff) : desc_kmajor(a_lo + aoff);
+            const uint64_t dbh = desc_mnmajor(b_hi + boff);
+            const uint64_t dbl = desc_mnmajor(b_lo + boff);
+            mma_tf32(d, dal, dbh, idesc, (chunk_first && kk == 0) ? 0u : 1u);
+            mma_tf32(d, dah, dbl, idesc, 1u);
+            mma_tf32(d, dah, dbh, idesc, 1u);
+          }
+          mma_commit(empty(s));
+          if (chunk_last) mma_commit(chunk_full(b));
+        }
+      }
+    } else {
+      // ---------------- lo converters (warps 2..7)
+      const int t = threadIdx.x - kConvWarp0 * 32;
       for (int it = 0; it < nk; ++it) {
         const int s = it % S;
-        if (!mbar_wait(empty(s), ((it / S) & 1) ^ 1, abort_flag)) break;
+        if (!mbar_wait(full(s), (it / S) & 1, abort_flag)) break;
         uint8_t* st = stage_ptr(s);
-        const int k0 = (kb_begin + it) * BK;
-        mbar_expect_tx(full(s), CF::A_BYTES + CF::B_BYTES);
-        if (TRANS_A) {
-#pragma unroll
-          for (int j = 0; j < BM / 32; ++j)
-            tma_load_3d(smem_u32(st + j * 4096), &tmA, full(s), m0 + 32 * j, k0, batch);
-        } else {
-          tma_load_3d(smem_u32(st), &tmA, full(s), k0, m0, batch);
-        }
-#pragma unroll
-        for (int j = 0; j < BN / 32; ++j)
-          tma_load_3d(smem_u32(st + CF::A_BYTES + j * 4096), &tmB, full(s), n0 + 32 * j, k0, batch);
-        ++issued;
+        lo_buffer(reinterpret_cast<const float4*>(st),
+                  reinterpret_cast<float4*>(st + CF::A_BYTES + CF::B_BYTES), CF::A_BYTES / 16, t);
+        lo_buffer(reinterpret_cast<const float4*>(st + CF::A_BYTES),
+                  reinterpret_cast<float4*>(st + 2 * CF::A_BYTES + CF::B_BYTES), CF::B_BYTES / 16, t);
+        fence_proxy_async();
+        mbar_arrive(conv(s));
       }
-      // drain: every issued load must land before the CTA may exit
-      for (int it = max(issued - S, 0); it < issued; ++it) {
-        const int s = it % S;
-        const uint64_t t0 = globaltimer();
-        while (!mbar_try_wait(full(s), (it / S) & 1)) {
-          if (globaltimer() - t0 > kWaitLimitNs) break;
-        }
-      }
-    }
-  } else if (warp == 1) {
-    // ---------------- MMA issuer
-    if (lane == 0) {
-      constexpr uint32_t idesc = make_idesc(BM, BN, TRANS_A);
-      for (int it = 0; it < nk; ++it) {
-        const int s = it % S;
-        if (!mbar_wait(conv(s), (it / S) & 1, abort_flag)) break;
-        tc_fence_after();
-        uint8_t* st = stage_ptr(s);
-        const uint32_t a_hi = smem_u32(st);
-        const uint32_t b_hi = a_hi + CF::A_BYTES;
-        const uint32_t a_lo = b_hi + CF::B_BYTES;
-        const uint32_t b_lo = a_lo + CF::A_BYTES;
-#pragma unroll
-        for (int kk = 0; kk < BK / 8; ++kk) {
-          // K step of 8 tf32: +32 B inside the K-major swizzle row, or +8 rows
-          // (1024 B) in the MN-major layout.
-          const uint32_t aoff = TRANS_A ? kk * 1024 : kk * 32;
-          const uint32_t boff = kk * 1024;
-          const uint64_t dah = TRANS_A ? desc_mnmajor(a_hi + aoff) : desc_kmajor(a_hi + aoff);
-          const uint64_t dal = TRANS_A ? desc_mnmajor(a_lo + aoff) : desc_kmajor(a_lo + aoff);
-          const uint64_t dbh = desc_mnmajor(b_hi + boff);
-          const uint64_t dbl = desc_mnmajor(b_lo + boff);
-          mma_tf32(tmem, dal, dbh, idesc, (it > 0 || kk > 0) ? 1u : 0u);
-          mma_tf32(tmem, dah, dbl, idesc, 1u);
-          mma_tf32(tmem, dah, dbh, idesc, 1u);
-        }
-        mma_commit(empty(s));
-      }
-      mma_commit(acc_bar);
     }
   } else {
-    // ---------------- split converters (warps 2..5)
-    const int t = threadIdx.x - 64;
-    for (int it = 0; it < nk; ++it) {
-      const int s = it % S;
-      if (!mbar_wait(full(s), (it / S) & 1, abort_flag)) break;
-      uint8_t* st = stage_ptr(s);
-      split_buffer(reinterpret_cast<float4*>(st), reinterpret_cast<float4*>(st + CF::A_BYTES + CF::B_BYTES),
-                   CF::A_BYTES / 16, t);
-      split_buffer(reinterpret_cast<float4*>(st + CF::A_BYTES),
-                   reinterpret_cast<float4*>(st + 2 * CF::A_BYTES + CF::B_BYTES), CF::B_BYTES / 16, t);
-      fence_proxy_async();
-      mbar_arrive(conv(s));
+    setmaxnreg_inc192();
+    // ---------------- promotion + epilogue (warps 8..15)
+    const int pw = warp - kPromoWarp0;
+    const int q = warp & 3;                         // TMEM lane quarter this warp may access
+    const int col_base = (pw >> 2) * CF::COLS_PER_WARP;
+    constexpr int NCOL = CF::COLS_PER_WARP;
+    float tot[NCOL];
+#pragma unroll
+    for (int j = 0; j < NCOL; ++j) tot[j] = 0.0f;
+    bool ok = true;
+    for (int c = 0; c < nchunks; ++c) {
+      const int b = c & 1;
+      ok = __all_sync(0xffffffffu, mbar_wait(chunk_full(b), (c >> 1) & 1, abort_flag));
+      if (!ok) break;
+      tc_fence_after();
+      const uint32_t base = tmem + ((uint32_t)(q * 32) << 16) + (uint32_t)(b * BN + col_base);
+#pragma unroll
+      for (int j = 0; j < NCOL / 32; ++j) {
+        uint32_t r[32];
+        tmem_ld32(base + j * 32, r);
+        tmem_ld_wait();
+#pragma unroll
+        for (int i = 0; i < 32; ++i) tot[j * 32 + i] += __uint_as_float(r[i]);
+      }
+      tc_fence_before();
+      mbar_arrive(chunk_empty(b));
     }
-    // ---------------- epilogue
-    // warp-uniform: tcgen05.ld below must be executed by all 32 lanes
-    const bool ok = __all_sync(0xffffffffu, (nk == 0) || mbar_wait(acc_bar, 0, abort_flag));
-    tc_fence_after();
-    const int q = warp & 3;  // TMEM lane quarter this warp may access
     const int row = m0 + q * 32 + lane;
     float* out = p.C + (int64_t)batch * p.batch_stride_c;
     int64_t ldo = p.ldc;
@@ -371,31 +422,18 @@ gemm3x_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ C
       out = p.C + (int64_t)z * p.M * p.N;
       ldo = p.N;
     }
-    float* orow = out + (int64_t)row * ldo;
-    const bool vec = ((ldo & 3) == 0) && ((reinterpret_cast<uintptr_t>(out) & 15) == 0);
-#pragma unroll 1
-    for (int c = 0; c < BN / 32; ++c) {
-      uint32_t r[32];
-      if (nk > 0 && ok) {
-        tmem_ld32(tmem + ((uint32_t)(q * 32) << 16) + c * 32, r);
-        tmem_ld_wait();
+    if (ok && row < p.M) {
+      float* orow = out + (int64_t)row * ldo;
+      const int col0 = n0 + col_base;
+      const bool vec = ((ldo & 3) == 0) && ((reinterpret_cast<uintptr_t>(out) & 15) == 0);
+      if (vec && col0 + NCOL <= p.N) {
+#pragma unroll
+        for (int j = 0; j < NCOL; j += 4)
+          *reinterpret_cast<float4*>(orow + col0 + j) = make_float4(tot[j], tot[j + 1], tot[j + 2], tot[j + 3]);
       } else {
 #pragma unroll
-        for (int j = 0; j < 32; ++j) r[j] = 0u;
-      }
-      const int col0 = n0 + c * 32;
-      if (row < p.M && ok) {
-        if (vec && col0 + 32 <= p.N) {
-#pragma unroll
-          for (int j = 0; j < 32; j += 4)
-            *reinterpret_cast<float4*>(orow + col0 + j) =
-                make_float4(__uint_as_float(r[j]), __uint_as_float(r[j + 1]),
-                            __uint_as_float(r[j + 2]), __uint_as_float(r[j + 3]));
-        } else {
-#pragma unroll
-          for (int j = 0; j < 32; ++j)
-            if (col0 + j < p.N) orow[col0 + j] = __uint_as_float(r[j]);
-        }
+        for (int j = 0; j < NCOL; ++j)
+          if (col0 + j < p.N) orow[col0 + j] = tot[j];
       }
     }
   }
@@ -403,7 +441,7 @@ gemm3x_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ C
   __syncthreads();
   if (warp == 1) {
     tc_fence_after();
-    tmem_dealloc(tmem, BN);
+    tmem_dealloc(tmem, CF::TMEM_COLS);
   }
 }
 
@@ -462,20 +500,21 @@ EncodeFn encode_fn() {
   return fn;
 }
 
-// 3-D fp32 tensor map {inner, outer, batch}, box {32, box_outer, 1}.  K-major
-// operands use the 128B swizzle (16-byte atoms), MN-major operands the 128B
-// swizzle with 32-byte atoms, which is the layout TF32 UMMA reads MN-major.
+// 3-D fp32 tensor map {inner, outer, batch}, box {box_inner, box_outer, 1}.
+// K-major operands (box_inner 16 = 64 B) use the 64B swizzle; MN-major
+// operands (box_inner 32 = 128 B) the 128B swizzle with 32-byte atoms, the
+// only MN-major layout TF32 UMMA reads.
 int make_map(CUtensorMap* tm, const float* base, int64_t inner, int64_t outer, int64_t batch,
              int64_t row_stride_elems, int64_t batch_stride_elems, int box_outer, bool mn_major) {
   EncodeFn enc = encode_fn();
   KB_REQUIRE(enc != nullptr, KB_ERR_CUDA, "cuTensorMapEncodeTiled unavailable");
   cuuint64_t dims[3] = {(cuuint64_t)inner, (cuuint64_t)outer, (cuuint64_t)batch};
   cuuint64_t strides[2] = {(cuuint64_t)row_stride_elems * 4, (cuuint64_t)batch_stride_elems * 4};
-  cuuint32_t box[3] = {32, (cuuint32_t)box_outer, 1};
+  cuuint32_t box[3] = {mn_major ? 32u : (cuuint32_t)BK, (cuuint32_t)box_outer, 1};
   cuuint32_t estr[3] = {1, 1, 1};
   CUresult r = enc(tm, CU_TENSOR_MAP_DATA_TYPE_FLOAT32, 3, const_cast<float*>(base), dims, strides, box, estr,
                    CU_TENSOR_MAP_INTERLEAVE_NONE,
-                   mn_major ? CU_TENSOR_MAP_SWIZZLE_128B_ATOM_32B : CU_TENSOR_MAP_SWIZZLE_128B,
+                   mn_major ? CU_TENSOR_MAP_SWIZZLE_128B_ATOM_32B : CU_TENSOR_MAP_SWIZZLE_64B,
                    CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
   KB_REQUIRE(r == CUDA_SUCCESS, KB_ERR_CUDA, "cuTensorMapEncodeTiled failed (%d)", (int)r);
   return KB_OK;
@@ -526,11 +565,11 @@ int run_gemm(const GemmArgs& g, int splits, float* ws, cudaStream_t s) {
   const int BN = bn256 ? 256 : 128;
   CUtensorMap ta, tb;
   if (g.trans_a) {
-    if (int st = make_map(&ta, g.A, g.M, g.K, g.batch, g.lda, g.sA, 32, true)) return st;
+    if (int st = make_map(&ta, g.A, g.M, g.K, g.batch, g.lda, g.sA, BK, true)) return st;
   } else {
     if (int st = make_map(&ta, g.A, g.K, g.M, g.batch, g.lda, g.sA, BM, false)) return st;
   }
-  if (int st = make_map(&tb, g.B, g.N, g.K, g.batch, g.ldb, g.sB, 32, true)) return st;
+  if (int st = make_map(&tb, g.B, g.N, g.K, g.batch, g.ldb, g.sB, BK, true)) return st;
   const int nk = (int)ceil_div(g.K, BK);
   Params p{};
   p.M = (int)g.M;
