@@ -2,14 +2,19 @@
 // log-softmax over the last dimension, plus the channel-dim RMSNorm form.
 //
 // Design (B200): a row is read from HBM exactly once into registers
-// (VPT float4 per thread, 128-bit streaming loads), reduced on chip, and
-// written once.  Rows up to 16K floats live in one CTA; longer rows are split
-// across a thread-block cluster of CL CTAs whose partial statistics are
-// combined through distributed shared memory (DSMEM), so even a 128 KB
-// softmax row never round-trips through global memory.  Rows up to 1K floats
-// use one warp per row (shuffle-only reductions).  Shapes outside these
-// register-resident paths (cols % 4 != 0, unaligned views, > 128K columns)
-// take a generic multi-pass kernel.
+// (VPT float4 per thread, 128-bit loads), reduced on chip, and written once.
+//   <= 1K floats   one warp per row, shuffle-only reductions;
+//   <= 16K floats  one CTA per row, several CTAs per SM overlapping their
+//                  load / reduce / store phases;
+//   <= 128K floats a persistent kernel: one 1024-thread CTA per SM (or a
+//                  2/4-CTA cluster per row beyond 32K floats, partial
+//                  statistics exchanged through DSMEM) holds the current row
+//                  in registers while the next row streams into shared
+//                  memory through a cp.async.bulk copy, so HBM keeps busy
+//                  during the reductions (a 128 KB softmax row is too large
+//                  for several rows per SM to overlap otherwise).
+// Other shapes (cols % 4 != 0, unaligned views, > 128K columns) take a
+// generic multi-pass kernel.
 //
 // Two-pass statistics are done on the register copy: LayerNorm computes the
 // mean, then sum((x - mean)^2) — never E[x^2] - mean^2 (the cancellation-prone
@@ -24,6 +29,8 @@ namespace kb {
 namespace {
 
 enum RowOp { kLayerNorm = 0, kRmsNorm = 1, kSoftmax = 2, kLogSoftmax = 3 };
+
+constexpr float kLog2e = 1.4426950408889634f;  // log2(e)
 
 struct RowArgs {
   const float* x;
@@ -89,7 +96,7 @@ struct ClusterReducer {
 template <RowOp OP, int VPT, class R>
 __device__ __forceinline__ void row_math(float4 (&v)[VPT], const bool (&ok)[VPT],
                                          const RowArgs& a, float4* yrow, int64_t col4_base,
-                                         int stride, int lane, const R& red) {
+                                         int stride, int lane, const R& red, bool store = true) {
   const float inv_cols = 1.0f / (float)a.cols;
   if constexpr (OP == kLayerNorm) {
     float s = 0.0f;
@@ -110,7 +117,7 @@ __device__ __forceinline__ void row_math(float4 (&v)[VPT], const bool (&ok)[VPT]
     const float4* b4 = reinterpret_cast<const float4*>(a.beta);
 #pragma unroll
     for (int k = 0; k < VPT; ++k)
-      if (ok[k]) {
+      if (ok[k] && store) {
         const int64_t c4 = col4_base + (int64_t)k * stride + lane;
         float4 r;
         r.x = (v[k].x - mean) * rstd;
@@ -137,7 +144,7 @@ __device__ __forceinline__ void row_math(float4 (&v)[VPT], const bool (&ok)[VPT]
     const float4* g4 = reinterpret_cast<const float4*>(a.gamma);
 #pragma unroll
     for (int k = 0; k < VPT; ++k)
-      if (ok[k]) {
+      if (ok[k] && store) {
         const int64_t c4 = col4_base + (int64_t)k * stride + lane;
         float4 r;
         r.x = v[k].x * inv;
@@ -156,22 +163,24 @@ __device__ __forceinline__ void row_math(float4 (&v)[VPT], const bool (&ok)[VPT]
     for (int k = 0; k < VPT; ++k)
       if (ok[k]) m = fmaxf(m, fmaxf(fmaxf(v[k].x, v[k].y), fmaxf(v[k].z, v[k].w)));
     m = red.max(m, 0);
+    // exp(x - m) = 2^(x log2(e) - m log2(e)): one FMA and exp2f per element
+    const float ml = (m == -INFINITY) ? 0.0f : m * kLog2e;
     float s = 0.0f;
     if constexpr (OP == kSoftmax) {
       // keep exp(x - m) in registers: exp is evaluated once per element
 #pragma unroll
       for (int k = 0; k < VPT; ++k)
         if (ok[k]) {
-          v[k].x = expf(v[k].x - m);
-          v[k].y = expf(v[k].y - m);
-          v[k].z = expf(v[k].z - m);
-          v[k].w = expf(v[k].w - m);
+          v[k].x = exp2f(fmaf(v[k].x, kLog2e, -ml));
+          v[k].y = exp2f(fmaf(v[k].y, kLog2e, -ml));
+          v[k].z = exp2f(fmaf(v[k].z, kLog2e, -ml));
+          v[k].w = exp2f(fmaf(v[k].w, kLog2e, -ml));
           s += (v[k].x + v[k].y) + (v[k].z + v[k].w);
         }
       const float inv = 1.0f / red.sum(s, 1);
 #pragma unroll
       for (int k = 0; k < VPT; ++k)
-        if (ok[k]) {
+        if (ok[k] && store) {
           float4 r = make_float4(v[k].x * inv, v[k].y * inv, v[k].z * inv, v[k].w * inv);
           st_stream(yrow + (int64_t)k * stride + lane, r);
         }
@@ -179,11 +188,12 @@ __device__ __forceinline__ void row_math(float4 (&v)[VPT], const bool (&ok)[VPT]
 #pragma unroll
       for (int k = 0; k < VPT; ++k)
         if (ok[k])
-          s += (expf(v[k].x - m) + expf(v[k].y - m)) + (expf(v[k].z - m) + expf(v[k].w - m));
+          s += (exp2f(fmaf(v[k].x, kLog2e, -ml)) + exp2f(fmaf(v[k].y, kLog2e, -ml))) +
+               (exp2f(fmaf(v[k].z, kLog2e, -ml)) + exp2f(fmaf(v[k].w, kLog2e, -ml)));
       const float lse = logf(red.sum(s, 1));
 #pragma unroll
       for (int k = 0; k < VPT; ++k)
-        if (ok[k]) {
+        if (ok[k] && store) {
           float4 r = make_float4((v[k].x - m) - lse, (v[k].y - m) - lse, (v[k].z - m) - lse,
                                  (v[k].w - m) - lse);
           st_stream(yrow + (int64_t)k * stride + lane, r);
@@ -220,6 +230,148 @@ __global__ void __launch_bounds__(NT) row_block_kernel(RowArgs a) {
   // would stall on them.
   if constexpr (CL > 1)
     asm volatile("barrier.cluster.arrive.relaxed.aligned;\n\tbarrier.cluster.wait.aligned;" ::: "memory");
+}
+
+// ---------------------------------------------------------------------------
+// Persistent variant with a bulk-copy prefetch.  A cluster of CL CTAs walks
+// rows cluster_id, cluster_id + nclusters, ...; CTA `rank` owns one
+// contiguous segment of each row.  The segment of the next row is fetched
+// into shared memory by cp.async.bulk (one 1-D bulk copy, completion counted
+// on an mbarrier) as soon as the current row has been moved into registers,
+// so HBM keeps streaming while the row is reduced, exchanged across the
+// cluster and written back.
+// Abort handling stays cluster-uniform: a CTA whose bounded wait expires
+// raises the fault word, stops copying and storing, but keeps executing the
+// per-row cluster barriers so its peers never wait on a CTA that left.
+// ---------------------------------------------------------------------------
+__device__ int g_row_fault = 0;
+
+__device__ __forceinline__ uint32_t smem_addr(const void* p) {
+  return static_cast<uint32_t>(__cvta_generic_to_shared(p));
+}
+__device__ __forceinline__ bool mbar_try_wait_parity(uint32_t bar, uint32_t parity) {
+  uint32_t ok;
+  asm volatile(
+      "{\n\t.reg .pred p;\n\t"
+      "mbarrier.try_wait.parity.shared::cta.b64 p, [%1], %2;\n\t"
+      "selp.u32 %0, 1, 0, p;\n\t}"
+      : "=r"(ok)
+      : "r"(bar), "r"(parity)
+      : "memory");
+  return ok != 0;
+}
+__device__ __forceinline__ uint64_t global_ns() {
+  uint64_t t;
+  asm volatile("mov.u64 %0, %%globaltimer;" : "=l"(t));
+  return t;
+}
+__device__ __forceinline__ bool wait_bounded(uint32_t bar, uint32_t parity) {
+  if (mbar_try_wait_parity(bar, parity)) return true;
+  const uint64_t t0 = global_ns();
+  for (uint32_t n = 1;; ++n) {
+    if (mbar_try_wait_parity(bar, parity)) return true;
+    if ((n & 63) == 0 && global_ns() - t0 > 2000000000ull) return false;
+  }
+}
+__device__ __forceinline__ void bulk_load(uint32_t dst, const void* src, uint32_t bytes, uint32_t bar) {
+  asm volatile("mbarrier.arrive.expect_tx.shared::cta.b64 _, [%0], %1;" ::"r"(bar), "r"(bytes) : "memory");
+  asm volatile(
+      "cp.async.bulk.shared::cluster.global.mbarrier::complete_tx::bytes [%0], [%1], %2, [%3];" ::"r"(dst),
+      "l"(src), "r"(bytes), "r"(bar)
+      : "memory");
+}
+
+template <RowOp OP, int NT, int VPT, int CL, int DEPTH>
+__global__ void __launch_bounds__(NT) row_persist_kernel(RowArgs a) {
+  extern __shared__ float4 seg_buf[];  // DEPTH segment buffers
+  __shared__ float red[32];
+  __shared__ float slots[2];
+  __shared__ __align__(8) uint64_t bars[DEPTH];
+  int rank = 0;
+  if constexpr (CL > 1) rank = (int)cg::this_cluster().block_rank();
+  const int64_t cluster_id = blockIdx.x / CL, nclusters = gridDim.x / CL;
+  const int seg4 = a.cols / 4 / CL;
+  const uint32_t seg_bytes = (uint32_t)seg4 * 16u;
+  const int64_t col4_base = (int64_t)rank * seg4;
+  const float* xseg = a.x + col4_base * 4;
+  if (threadIdx.x == 0) {
+    for (int d = 0; d < DEPTH; ++d)
+      asm volatile("mbarrier.init.shared::cta.b64 [%0], 1;" ::"r"(smem_addr(&bars[d])) : "memory");
+    asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
+  }
+  __syncthreads();
+  if constexpr (CL > 1) cg::this_cluster().sync();  // peers' shared memory exists from here on
+  // prologue: the first DEPTH rows of this cluster in flight
+  if (threadIdx.x == 0)
+    for (int d = 0; d < DEPTH; ++d) {
+      const int64_t rr = cluster_id + (int64_t)d * nclusters;
+      if (rr < a.rows)
+        bulk_load(smem_addr(seg_buf + (size_t)d * seg4), xseg + rr * (int64_t)a.cols, seg_bytes,
+                  smem_addr(&bars[d]));
+    }
+  bool alive = true;
+  ClusterReducer<NT, CL> r{red, slots};
+  int64_t i = 0;
+  for (int64_t row = cluster_id; row < a.rows; row += nclusters, ++i) {
+    const int slot = (int)(i % DEPTH);
+    const uint32_t parity = (uint32_t)((i / DEPTH) & 1);
+    const float4* buf = seg_buf + (size_t)slot * seg4;
+    bool got = alive ? wait_bounded(smem_addr(&bars[slot]), parity) : true;
+    float4 v[VPT];
+    bool ok[VPT];
+#pragma unroll
+    for (int k = 0; k < VPT; ++k) {
+      const int j = k * NT + threadIdx.x;
+      ok[k] = j < seg4;
+      v[k] = (ok[k] && alive && got) ? buf[j] : make_float4(0.f, 0.f, 0.f, 0.f);
+    }
+    // everyone has read the buffer (and agrees whether the copy landed)
+    got = __syncthreads_and(got) != 0;
+    if (!got && alive) {
+      alive = false;
+      if (threadIdx.x == 0) atomicExch(&g_row_fault, 1);
+    }
+    const int64_t next = row + (int64_t)DEPTH * nclusters;
+    if (threadIdx.x == 0 && alive && next < a.rows)
+      bulk_load(smem_addr(buf), xseg + next * (int64_t)a.cols, seg_bytes, smem_addr(&bars[slot]));
+    float4* ys = reinterpret_cast<float4*>(a.y + row * (int64_t)a.cols) + col4_base;
+    row_math<OP, VPT>(v, ok, a, ys, col4_base, NT, threadIdx.x, r, alive);
+  }
+  if constexpr (CL > 1)
+    asm volatile("barrier.cluster.arrive.relaxed.aligned;\n\tbarrier.cluster.wait.aligned;" ::: "memory");
+}
+
+template <RowOp OP, int NT, int VPT, int CL, int DEPTH>
+cudaError_t launch_persist(const RowArgs& a, cudaStream_t s) {
+  auto kern = row_persist_kernel<OP, NT, VPT, CL, DEPTH>;
+  const int smem = a.cols / CL * 4 * DEPTH;
+  static uint64_t attr_set = 0;
+  int dev = 0;
+  cudaGetDevice(&dev);
+  if (dev < 64 && !(attr_set >> dev & 1)) {
+    cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, 200 * 1024);
+    if (e != cudaSuccess) return e;
+    attr_set |= 1ull << dev;
+  }
+  cudaLaunchConfig_t cfg = {};
+  cfg.blockDim = dim3(NT);
+  cfg.dynamicSmemBytes = smem;
+  cfg.stream = s;
+  cudaLaunchAttribute attr[1];
+  attr[0].id = cudaLaunchAttributeClusterDimension;
+  attr[0].val.clusterDim.x = CL;
+  attr[0].val.clusterDim.y = 1;
+  attr[0].val.clusterDim.z = 1;
+  cfg.attrs = attr;
+  cfg.numAttrs = 1;
+  // resident clusters on the whole GPU, times CL CTAs each
+  int nclusters = 0;
+  cfg.gridDim = dim3(CL * 148);
+  cudaError_t e = cudaOccupancyMaxActiveClusters(&nclusters, kern, &cfg);
+  if (e != cudaSuccess || nclusters <= 0) nclusters = sm_count() / CL;
+  nclusters = (int)std::max<int64_t>(1, std::min<int64_t>(nclusters, a.rows));
+  cfg.gridDim = dim3((unsigned)(nclusters * CL));
+  return cudaLaunchKernelEx(&cfg, kern, a);
 }
 
 // One warp per row (rows of at most 32 * VPT * 4 floats); 4 warps per CTA.
@@ -347,12 +499,14 @@ int launch_rows(const char* name, const RowArgs& a, cudaStream_t s) {
     e = launch_block<OP, 256, 8, 1>(a, s);
   } else if (c <= 16384) {
     e = launch_block<OP, 512, 8, 1>(a, s);
-  } else if (c <= 32768 && c % 8 == 0) {
-    e = launch_block<OP, 512, 8, 2>(a, s);
-  } else if (c <= 65536 && c % 16 == 0) {
-    e = launch_block<OP, 512, 8, 4>(a, s);
-  } else if (c % 32 == 0) {
-    e = launch_block<OP, 512, 8, 8>(a, s);
+  } else if (c <= 32768) {
+    // one persistent 1024-thread CTA per SM: the row in registers, the next
+    // row streaming into shared memory
+    e = launch_persist<OP, 1024, 8, 1, 1>(a, s);
+  } else if (c <= 65536 && c % 8 == 0) {
+    e = launch_persist<OP, 1024, 8, 2, 1>(a, s);
+  } else if (c % 16 == 0) {
+    e = launch_persist<OP, 1024, 8, 4, 1>(a, s);
   } else {
     row_generic_kernel<OP><<<(unsigned)a.rows, 512, 0, s>>>(a);
     e = cudaGetLastError();
