@@ -322,7 +322,34 @@ def profile_op(op: str, frac: float, reps: int = 3) -> int:
 
 
 # ----------------------------------------------------------------- main
+class _StdoutToStderr:
+    """Send everything written to fd 1 (including C-level prints such as
+    NCCL's version banner) to stderr, so the result line is the only thing
+    on stdout; `emit` writes to the original stdout."""
+
+    def __enter__(self):
+        sys.stdout.flush()
+        self._saved = os.dup(1)
+        os.dup2(2, 1)
+        return self
+
+    def emit(self, line: str):
+        sys.stdout.flush()
+        os.write(self._saved, (line + "\n").encode())
+
+    def __exit__(self, *exc):
+        sys.stdout.flush()
+        os.dup2(self._saved, 1)
+        os.close(self._saved)
+        return False
+
+
 def main() -> int:
+    with _StdoutToStderr() as out:
+        return _main(out)
+
+
+def _main(out) -> int:
     ap = argparse.ArgumentParser()
     ap.add_argument("--gpus", type=int, default=1)
     ap.add_argument("--steps", type=int, default=200)
@@ -364,11 +391,11 @@ def main() -> int:
                 "cpu_baseline": {k: r[k] for k in ("value", "unit", "cores", "kind", "sample")},
                 "e2e": {"value": r["value"], "unit": "GB/s", "h2d_bytes_per_step": 0,
                         "d2h_bytes_per_step": 0}}
-        print(json.dumps(line), flush=True)
+        out.emit(json.dumps(line))
         return 0
 
     if not torch.cuda.is_available():
-        print(json.dumps({"error": "no CUDA device"}))
+        out.emit(json.dumps({"error": "no CUDA device"}))
         return 1
     torch.cuda.set_device(local_rank)
     device = torch.device("cuda", local_rank)
@@ -508,7 +535,7 @@ def main() -> int:
         "gpu_launches": a.steps * sum(LAUNCHES[n] for n in ops), "per_op": per_op,
         "impl": "ours",
     }
-    print(json.dumps(line), flush=True)
+    out.emit(json.dumps(line))
     return 0
 
 

@@ -1,0 +1,101 @@
+"""GPU, 2 ranks over NCCL: the sharded ops of kbb200.dist with the CUDA
+per-shard kernels reproduce the single-device answer on the global input.
+
+Each rank builds the same seeded global tensors on the CPU, keeps its shard
+on its own GPU, runs the sharded op (local partial kernel, one all_reduce,
+local finishing kernel) and compares with the oracle on the whole input.
+Skipped unless the process sees at least 2 GPUs.  NVLS is switched off (plain
+NCCL rings over NVLink).
+"""
+from __future__ import annotations
+
+import datetime
+import os
+import socket
+import sys
+import traceback
+from pathlib import Path
+
+import numpy as np
+import pytest
+import torch
+import torch.multiprocessing as mp
+
+pytestmark = pytest.mark.gpu
+REPO = Path(__file__).resolve().parent.parent
+
+
+def _free_port() -> int:
+    with socket.socket() as s:
+        s.bind(("127.0.0.1", 0))
+        return s.getsockname()[1]
+
+
+def _worker(rank, world, port, q):
+    try:
+        for p in (str(REPO), str(REPO / "kernelbench-hip_b200")):
+            if p not in sys.path:
+                sys.path.insert(0, p)
+        os.environ.update(MASTER_ADDR="127.0.0.1", MASTER_PORT=str(port), NCCL_NVLS_ENABLE="0")
+        torch.cuda.set_device(rank)
+        dev = torch.device("cuda", rank)
+        import torch.distributed as tdist
+
+        tdist.init_process_group("nccl", rank=rank, world_size=world, device_id=dev,
+                                 timeout=datetime.timedelta(seconds=60))
+        from kbb200 import dist
+        from oracle import ops as O
+
+        res = {}
+        g = torch.Generator().manual_seed(7)
+        a, b = torch.randn(1 << 20, generator=g), torch.randn(1 << 20, generator=g)
+        got = dist.mse_loss(dist.shard(a, rank, world).to(dev), dist.shard(b, rank, world).to(dev),
+                            total_n=a.numel())
+        res["mse"] = (float(got), float(O.mse_loss(a.numpy(), b.numpy())), 1e-3)
+
+        x = torch.randn(8, 64, 130, generator=g)
+        got = dist.frobenius_normalize(dist.shard(x, rank, world).to(dev)).cpu().numpy()
+        lo, hi = dist.shard_range(8, rank, world)
+        res["frobenius"] = (got, O.frobenius_normalize(x.numpy())[lo:hi], 1e-5)
+
+        x = torch.randn(6, 32, 20, 24, generator=g) * 2 + 1
+        w, bb = 1 + 0.02 * torch.randn(32, generator=g), 0.02 * torch.randn(32, generator=g)
+        got = dist.batch_norm_train(dist.shard(x, rank, world).to(dev), w.to(dev), bb.to(dev)).cpu().numpy()
+        lo, hi = dist.shard_range(6, rank, world)
+        res["batchnorm"] = (got, O.batch_norm_train(x.numpy(), w.numpy(), bb.numpy())[lo:hi], 1e-5)
+
+        A, B = torch.randn(256, 65536, generator=g), torch.randn(65536, 256, generator=g)
+        got = dist.matmul_splitk(dist.shard(A, rank, world, dim=1).contiguous().to(dev),
+                                 dist.shard(B, rank, world, dim=0).contiguous().to(dev)).cpu().numpy()
+        res["splitk"] = (got, O.matmul(A.numpy(), B.numpy()), 1e-3)
+        torch.cuda.synchronize()
+        tdist.destroy_process_group()
+        q.put((rank, "ok", res))
+    except Exception as e:
+        q.put((rank, "err", f"{type(e).__name__}: {e}\n{traceback.format_exc()[-600:]}"))
+
+
+def test_sharded_ops_on_two_gpus():
+    if torch.cuda.device_count() < 2:
+        pytest.skip("needs 2 GPUs")
+    world = 2
+    ctx = mp.get_context("spawn")
+    q = ctx.Queue()
+    port = _free_port()
+    procs = [ctx.Process(target=_worker, args=(r, world, port, q)) for r in range(world)]
+    for p in procs:
+        p.start()
+    out = {}
+    try:
+        for _ in range(world):
+            rank, status, res = q.get(timeout=300)
+            out[rank] = (status, res)
+    finally:
+        for p in procs:
+            p.join(timeout=60)
+            if p.is_alive():
+                p.kill()
+    for rank, (status, res) in out.items():
+        assert status == "ok", res
+        for name, (got, want, tol) in res.items():
+            np.testing.assert_allclose(got, want, rtol=tol, atol=tol, err_msg=f"rank {rank} {name}")
