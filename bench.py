@@ -45,7 +45,8 @@ FALLBACK_BF16_TFLOPS = 1590.0
 LAUNCHES = {"gelu_tanh": 1, "gelu_erf": 1, "swish": 1, "relu": 1, "layer_norm": 1, "rms_norm": 1,
             "softmax": 1, "log_softmax": 1, "sum_dim": 1, "mean_dim": 1, "argmax_dim": 1,
             "mse_loss": 2, "frobenius_normalize": 2, "max_pool2d": 1, "batch_norm_train": 2,
-            "matmul": 1, "bmm": 1, "matmul_splitk": 2, "gemv": 1}
+            "matmul": 1, "bmm": 1, "matmul_splitk": 2, "gemv": 1, "matmul_transposed_a": 1,
+            "matmul_symmetric": 1, "diag_matmul": 1, "matmul_small_k": 1}
 
 # DRAM bytes per full-size launch (dram__bytes_read.sum + dram__bytes_write.sum)
 # from the ncu captures summarised in profiles/: captured on a quarter of the
@@ -212,6 +213,15 @@ def make_runner(name: str, inputs: list, world: int, rank: int):
     if name == "gemv":
         y = torch.empty(x.shape[0], device=x.device)
         return (lambda: K.gemv(x, inputs[1], out=y)), y
+    if name == "matmul_transposed_a":
+        y = torch.empty(x.shape[1], inputs[1].shape[1], device=x.device)
+        return (lambda: K.matmul(x, inputs[1], trans_a=True, out=y)), y
+    if name in ("matmul_symmetric", "matmul_small_k"):
+        y = torch.empty(x.shape[0], inputs[1].shape[1], device=x.device)
+        return (lambda: K.matmul(x, inputs[1], out=y)), y
+    if name == "diag_matmul":
+        y = torch.empty_like(inputs[1])
+        return (lambda: K.diag_matmul(x, inputs[1], out=y)), y
     raise KeyError(name)
 
 
@@ -345,11 +355,11 @@ class _StdoutToStderr:
 
 
 def main() -> int:
-    with _StdoutToStderr() as out:
-        return _main(out)
+    with _StdoutToStderr() as sink:
+        return _main(sink)
 
 
-def _main(out) -> int:
+def _main(sink) -> int:
     ap = argparse.ArgumentParser()
     ap.add_argument("--gpus", type=int, default=1)
     ap.add_argument("--steps", type=int, default=200)
@@ -391,11 +401,11 @@ def _main(out) -> int:
                 "cpu_baseline": {k: r[k] for k in ("value", "unit", "cores", "kind", "sample")},
                 "e2e": {"value": r["value"], "unit": "GB/s", "h2d_bytes_per_step": 0,
                         "d2h_bytes_per_step": 0}}
-        out.emit(json.dumps(line))
+        sink.emit(json.dumps(line))
         return 0
 
     if not torch.cuda.is_available():
-        out.emit(json.dumps({"error": "no CUDA device"}))
+        sink.emit(json.dumps({"error": "no CUDA device"}))
         return 1
     torch.cuda.set_device(local_rank)
     device = torch.device("cuda", local_rank)
@@ -535,7 +545,7 @@ def _main(out) -> int:
         "gpu_launches": a.steps * sum(LAUNCHES[n] for n in ops), "per_op": per_op,
         "impl": "ours",
     }
-    out.emit(json.dumps(line))
+    sink.emit(json.dumps(line))
     return 0
 
 

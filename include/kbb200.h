@@ -67,6 +67,12 @@ KB_API int kb_swish_f32(const float* x, float* y, int64_t n, kbStream stream);
 /* replaces relu_entry, candidates/19_ReLU/v1.py:15-20: y = max(x, 0)       */
 KB_API int kb_relu_f32(const float* x, float* y, int64_t n, kbStream stream);
 
+/* replaces diagmul_entry, candidates/12_Matmul_with_diagonal_matrices_/
+ * v1.py:19-27: y[i, j] = a[i] * b[i, j], i.e. diag(a) @ B for a[rows],
+ * b[rows, cols] — a broadcast row scale, never the rows x rows matrix.      */
+KB_API int kb_diag_matmul_f32(const float* a, const float* b, float* y,
+                              int64_t rows, int64_t cols, kbStream stream);
+
 /* ---- row normalisation over the last `cols` elements of each row ------ */
 /* replaces layernorm_entry, candidates/40_LayerNorm/v1.py:62-80.
  * gamma/beta may be NULL (identity affine).  Biased variance, eps inside

@@ -117,10 +117,51 @@ int launch_elementwise(const char* name, const float* x, float* y, int64_t n, cu
   return check_launch(name);
 }
 
+// y[i, j] = a[i] * b[i, j]: diag(a) @ B without the N x N matrix
+// (candidates/12_Matmul_with_diagonal_matrices_/v1.py:10-17).  cols % 4 == 0
+// and aligned pointers: each float4 lies in one row, a[row] comes from L1/L2.
+__global__ void __launch_bounds__(kThreads)
+row_scale_vec4_kernel(const float* __restrict__ a, const float4* __restrict__ b, float4* __restrict__ y,
+                      int64_t nvec, int64_t cols4) {
+  for (int64_t i = (int64_t)blockIdx.x * kThreads + threadIdx.x; i < nvec;
+       i += (int64_t)gridDim.x * kThreads) {
+    const float s = __ldg(a + i / cols4);
+    const float4 v = ld_stream(b + i);
+    st_stream(y + i, make_float4(s * v.x, s * v.y, s * v.z, s * v.w));
+  }
+}
+
+__global__ void __launch_bounds__(kThreads)
+row_scale_scalar_kernel(const float* __restrict__ a, const float* __restrict__ b, float* __restrict__ y,
+                        int64_t n, int64_t cols) {
+  for (int64_t i = (int64_t)blockIdx.x * kThreads + threadIdx.x; i < n; i += (int64_t)gridDim.x * kThreads)
+    y[i] = a[i / cols] * b[i];
+}
+
 }  // namespace
 }  // namespace kb
 
 extern "C" {
+
+int kb_diag_matmul_f32(const float* a, const float* b, float* y, int64_t rows, int64_t cols,
+                       kbStream stream) {
+  const char* name = "kb_diag_matmul_f32";
+  KB_REQUIRE(rows >= 0 && cols >= 0, KB_ERR_INVALID_ARG, "%s: negative size", name);
+  if (rows == 0 || cols == 0) return KB_OK;
+  KB_REQUIRE(a && b && y, KB_ERR_INVALID_ARG, "%s: null pointer", name);
+  const int64_t n = rows * cols;
+  const int grid_cap = kb::sm_count() * 8;
+  if (cols % 4 == 0 && kb::aligned16(b) && kb::aligned16(y)) {
+    const int64_t nvec = n / 4;
+    const int grid = (int)std::max<int64_t>(1, std::min<int64_t>(kb::ceil_div(nvec, kb::kThreads), grid_cap));
+    kb::row_scale_vec4_kernel<<<grid, kb::kThreads, 0, stream>>>(
+        a, reinterpret_cast<const float4*>(b), reinterpret_cast<float4*>(y), nvec, cols / 4);
+  } else {
+    const int grid = (int)std::max<int64_t>(1, std::min<int64_t>(kb::ceil_div(n, kb::kThreads), grid_cap));
+    kb::row_scale_scalar_kernel<<<grid, kb::kThreads, 0, stream>>>(a, b, y, n, cols);
+  }
+  return kb::check_launch(name);
+}
 
 int kb_gelu_tanh_f32(const float* x, float* y, int64_t n, kbStream stream) {
   return kb::launch_elementwise<kb::GeluTanh>("kb_gelu_tanh_f32", x, y, n, stream);

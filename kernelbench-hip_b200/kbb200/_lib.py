@@ -31,6 +31,7 @@ SIGNATURES: dict[str, tuple] = {
     "kb_gelu_erf_f32": (_int, [_p, _p, _i64, _p]),
     "kb_swish_f32": (_int, [_p, _p, _i64, _p]),
     "kb_relu_f32": (_int, [_p, _p, _i64, _p]),
+    "kb_diag_matmul_f32": (_int, [_p, _p, _p, _i64, _i64, _p]),
     "kb_layernorm_f32": (_int, [_p, _p, _p, _p, _i64, _i64, _float, _p]),
     "kb_rmsnorm_f32": (_int, [_p, _p, _p, _i64, _i64, _i64, _float, _p]),
     "kb_softmax_f32": (_int, [_p, _p, _i64, _i64, _p]),

@@ -136,3 +136,14 @@ def splitk_gemm_entry(A, B, C, split: int = 0) -> None:
 def gemv_entry(A, B, C) -> None:
     """candidates/4_Matrix_vector_multiplication_/v1.py:36 — C = A @ B, B [K] or [K, 1]."""
     ops.gemv(A, B, out=C)
+
+
+def diagmul_entry(a, b, y) -> None:
+    """candidates/12_Matmul_with_diagonal_matrices_/v1.py:19 — y = diag(a) @ b."""
+    ops.diag_matmul(a, b, out=y)
+
+
+def smallk_gemm_entry(A, B, C) -> None:
+    """candidates/7_Matmul_with_small_K_dimension_/v1.py — C = A @ B with a
+    small K; served by the 3xTF32 tcgen05 GEMM."""
+    ops.matmul(A, B, out=C)

@@ -18,7 +18,7 @@ from ._lib import LIB, check
 __all__ = [
     "gelu_tanh", "gelu_erf", "swish", "relu", "layer_norm", "rms_norm", "softmax",
     "log_softmax", "sum_dim", "mean_dim", "argmax_dim", "mse_loss", "frobenius_normalize",
-    "max_pool2d", "batch_norm_train", "matmul", "bmm", "matmul_splitk", "gemv",
+    "max_pool2d", "batch_norm_train", "matmul", "bmm", "matmul_splitk", "gemv", "diag_matmul",
     "mse_partial", "mse_finalize", "sumsq_partial", "scale_by_inv_norm", "batch_norm_stats",
     "batch_norm_apply",
 ]
@@ -97,6 +97,19 @@ def swish(x, out=None):
 def relu(x, out=None):
     """max(x, 0), NaN propagated — candidates/19_ReLU/v1.py:10-13."""
     return _elementwise("kb_relu_f32", x, out)
+
+
+def diag_matmul(a, b, out=None):
+    """diag(a) @ B as a broadcast row scale, y[i, j] = a[i] * b[i, j] —
+    replaces candidates/12_Matmul_with_diagonal_matrices_/v1.py:10-27."""
+    fn = "kb_diag_matmul_f32"
+    _check_f32(fn, a, b)
+    if a.dim() != 1 or b.dim() != 2 or b.shape[0] != a.shape[0]:
+        raise RuntimeError(f"{fn}: expected a[N], b[N, M], got {tuple(a.shape)} and {tuple(b.shape)}")
+    y = _out_like(b, out, fn)
+    check(fn, LIB.kb_diag_matmul_f32(a.data_ptr(), b.data_ptr(), y.data_ptr(), b.shape[0], b.shape[1],
+                                     _stream(b)))
+    return y
 
 
 # ---------------------------------------------------------------- row ops

@@ -99,6 +99,19 @@ WORKLOADS: dict[str, Workload] = {w.name: w for w in [
     Workload("gemv", "4_Matrix_vector_multiplication_", "gemm",
              (("A", (4096, 1048576), "normal"), ("x", (1048576,), "normal")),
              F32 * (4096 * 1048576 + 1048576 + 4096), flops=2 * 4096 * 1048576),
+    # the reference's remaining candidates (structured / shaped matmuls)
+    Workload("matmul_transposed_a", "16_Matmul_with_transposed_A", "structured",
+             (("A", (8192, 8192), "gemm_t"), ("B", (8192, 8192), "gemm")),
+             3 * F32 * 8192 * 8192, flops=2 * 8192 ** 3, bound="tensor"),
+    Workload("matmul_symmetric", "13_Matmul_for_symmetric_matrices", "structured",
+             (("A", (8192, 8192), "gemm_sym"), ("B", (8192, 8192), "gemm_sym")),
+             3 * F32 * 8192 * 8192, flops=2 * 8192 ** 3, bound="tensor"),
+    Workload("diag_matmul", "12_Matmul_with_diagonal_matrices_", "structured",
+             (("A", (4096,), "normal"), ("B", (4096, 4096), "normal")),
+             F32 * (4096 + 2 * 4096 * 4096)),
+    Workload("matmul_small_k", "7_Matmul_with_small_K_dimension_", "structured",
+             (("A", (32768, 64), "gemm"), ("B", (64, 32768), "gemm")),
+             F32 * (2 * 32768 * 64 + 32768 * 32768), flops=2 * 32768 * 32768 * 64),
 ]}
 
 FAMILIES = {
@@ -107,6 +120,7 @@ FAMILIES = {
     "reductions": ["sum_dim", "mean_dim", "argmax_dim", "mse_loss", "frobenius_normalize"],
     "spatial": ["max_pool2d", "batch_norm_train"],
     "gemm": ["matmul", "bmm", "matmul_splitk", "gemv"],
+    "structured": ["matmul_transposed_a", "matmul_symmetric", "diag_matmul", "matmul_small_k"],
 }
 
 
@@ -124,6 +138,11 @@ def fill_(t: torch.Tensor, dist: str, gen: torch.Generator, fan_in: int = 1) -> 
         return t.normal_(0.0, 0.02, generator=gen)
     if dist == "gemm":
         return t.normal_(0.0, 1.0 / math.sqrt(fan_in), generator=gen)
+    if dist == "gemm_t":  # A stored [K, M]
+        return t.normal_(0.0, 1.0 / math.sqrt(t.shape[0]), generator=gen)
+    if dist == "gemm_sym":  # symmetric, entries ~ N(0, 1/K)
+        t.normal_(0.0, 1.0 / math.sqrt(2.0 * t.shape[-1]), generator=gen)
+        return t.add_(t.T.clone())
     raise ValueError(dist)
 
 

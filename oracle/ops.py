@@ -212,3 +212,14 @@ def matmul_splitk(a, b):
 def gemv(a, x):
     """candidates/4_Matrix_vector_multiplication_/v1.py:14-34."""
     return _out(_f64(a) @ _f64(x))
+
+
+def diag_matmul(a, b):
+    """candidates/12_Matmul_with_diagonal_matrices_/v1.py:10-17: diag(a) @ B
+    evaluated as the row scale a[i] * b[i, j]."""
+    return _out(_f64(a)[:, None] * _f64(b))
+
+
+def matmul_transposed_a(a_t, b):
+    """candidates/16_Matmul_with_transposed_A/v1.py (TRANS_A): A stored [K, M], C = A^T @ B."""
+    return _out(_f64(a_t).T @ _f64(b))

@@ -145,6 +145,20 @@ class Matmul(nn.Module):
         return torch.matmul(A, B)
 
 
+class MatmulTransposedA(nn.Module):
+    """C = A^T @ B with A stored [K, M]."""
+
+    def forward(self, A, B):
+        return torch.matmul(A.T, B)
+
+
+class DiagMatmul(nn.Module):
+    """diag(A) @ B, evaluated as the broadcast row scale A[:, None] * B."""
+
+    def forward(self, A, B):
+        return A.unsqueeze(1) * B
+
+
 class Bmm(nn.Module):
     def forward(self, A, B):
         return torch.bmm(A, B)
@@ -197,6 +211,22 @@ PROBLEMS: dict[str, tuple] = {
                                         {"A": (64, 4099), "x": (4099,)}),
 }
 
+# the remaining candidates of the reference (structured and shaped matmuls)
+PROBLEMS.update({
+    "16_Matmul_with_transposed_A": (MatmulTransposedA, [], (("A", (8192, 8192), "gemm_t"),
+                                                           ("B", (8192, 8192), "gemm")),
+                                    {"A": (160, 96), "B": (160, 200)}),
+    "13_Matmul_for_symmetric_matrices": (Matmul, [], (("A", (8192, 8192), "gemm_sym"),
+                                                      ("B", (8192, 8192), "gemm_sym")),
+                                         {"A": (192, 192), "B": (192, 192)}),
+    "12_Matmul_with_diagonal_matrices_": (DiagMatmul, [], (("A", (4096,), "normal"),
+                                                           ("B", (4096, 4096), "normal")),
+                                          {"A": (67,), "B": (67, 300)}),
+    "7_Matmul_with_small_K_dimension_": (Matmul, [], (("A", (32768, 64), "gemm"),
+                                                      ("B", (64, 32768), "gemm")),
+                                         {"A": (300, 64), "B": (64, 520)}),
+})
+
 SUBSET = list(PROBLEMS)
 
 
@@ -214,6 +244,11 @@ def draw(shape, dist: str, fan_in: int = 1) -> torch.Tensor:
         return 0.02 * torch.randn(shape)
     if dist == "gemm":
         return torch.randn(shape) / math.sqrt(fan_in)
+    if dist == "gemm_t":  # A stored [K, M]: scaled by 1/sqrt(K) with K the leading dim
+        return torch.randn(shape) / math.sqrt(shape[0])
+    if dist == "gemm_sym":  # symmetric, entries ~ N(0, 1/K)
+        r = torch.randn(shape) / math.sqrt(shape[-1])
+        return (r + r.T) * (0.5 ** 0.5)
     raise ValueError(dist)
 
 
@@ -225,7 +260,7 @@ def input_spec(name: str, shapes: dict | str | None = None):
     out = []
     for nm, shape, dist in spec:
         shape = tuple(shapes.get(nm, shape))
-        if dist == "gemm":
+        if dist in ("gemm", "gemm_sym"):
             fan_in = shape[-2] if nm == "B" else shape[-1]
         else:
             fan_in = 1

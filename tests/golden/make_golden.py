@@ -44,6 +44,10 @@ GOLDEN_SHAPES = {
     "3_Batched_matrix_multiplication": {"A": (2, 32, 48), "B": (2, 48, 40)},
     "6_Matmul_with_large_K_dimension_": {"A": (16, 2048), "B": (2048, 24)},
     "4_Matrix_vector_multiplication_": {"A": (17, 1031), "x": (1031,)},
+    "16_Matmul_with_transposed_A": {"A": (72, 64), "B": (72, 48)},
+    "13_Matmul_for_symmetric_matrices": {"A": (64, 64), "B": (64, 64)},
+    "12_Matmul_with_diagonal_matrices_": {"A": (33,), "B": (33, 257)},
+    "7_Matmul_with_small_K_dimension_": {"A": (96, 64), "B": (64, 80)},
 }
 SEED = 0
 

@@ -34,6 +34,10 @@ ORACLE = {
     "3_Batched_matrix_multiplication": (lambda a, b: O.bmm(a, b), 1e-3),
     "6_Matmul_with_large_K_dimension_": (lambda a, b: O.matmul_splitk(a, b), 1e-3),
     "4_Matrix_vector_multiplication_": (lambda a, x: O.gemv(a, x), 1e-3),
+    "16_Matmul_with_transposed_A": (lambda a, b: O.matmul_transposed_a(a, b), 1e-3),
+    "13_Matmul_for_symmetric_matrices": (lambda a, b: O.matmul(a, b), 1e-3),
+    "12_Matmul_with_diagonal_matrices_": (lambda a, b: O.diag_matmul(a, b), 1e-5),
+    "7_Matmul_with_small_K_dimension_": (lambda a, b: O.matmul(a, b), 1e-3),
 }
 
 
@@ -61,6 +65,10 @@ def gpu_call(name: str):
         "3_Batched_matrix_multiplication": lambda a, b: K.bmm(a, b),
         "6_Matmul_with_large_K_dimension_": lambda a, b: K.matmul_splitk(a, b),
         "4_Matrix_vector_multiplication_": lambda a, x: K.gemv(a, x),
+        "16_Matmul_with_transposed_A": lambda a, b: K.matmul(a, b, trans_a=True),
+        "13_Matmul_for_symmetric_matrices": lambda a, b: K.matmul(a, b),
+        "12_Matmul_with_diagonal_matrices_": lambda a, b: K.diag_matmul(a, b),
+        "7_Matmul_with_small_K_dimension_": lambda a, b: K.matmul(a, b),
     }
     return table[name]
 

@@ -21,7 +21,8 @@ from tests.opmap import EXACT, ORACLE, assert_close, gpu_call, load_golden
 pytestmark = pytest.mark.gpu
 
 GEMMS = {"1_Square_matrix_multiplication_", "3_Batched_matrix_multiplication",
-         "6_Matmul_with_large_K_dimension_"}
+         "6_Matmul_with_large_K_dimension_", "16_Matmul_with_transposed_A",
+         "13_Matmul_for_symmetric_matrices", "7_Matmul_with_small_K_dimension_"}
 
 
 def _dev(arrs, device):
@@ -384,10 +385,12 @@ def test_gemm_full_size_vs_torch_fp32(name, cuda_device):
     w = next(w for w in WORKLOADS.values() if w.problem == name)
     A, B = make_inputs(w, cuda_device, seed=0)
     got = gpu_call(name)(A, B)
+    Model_ref = problems.load_problem(name)[0]
     prev = torch.backends.cuda.matmul.allow_tf32
     torch.backends.cuda.matmul.allow_tf32 = False
     try:
-        want = torch.bmm(A, B) if A.dim() == 3 else A @ B
+        with torch.no_grad():
+            want = Model_ref()(A, B)
     finally:
         torch.backends.cuda.matmul.allow_tf32 = prev
     assert torch.isclose(got, want, atol=1e-3, rtol=1e-3).all()
@@ -414,3 +417,12 @@ def test_gemm_accuracy_matches_fp32_cublas(mnk, cuda_device):
         torch.backends.cuda.matmul.allow_tf32 = prev
     e_ours = (K.matmul(A, B).double() - ref).abs().max().item()
     assert e_ours <= 4 * e_torch + 1e-6, f"3xTF32 max error {e_ours:.3e} vs fp32 {e_torch:.3e}"
+
+
+@pytest.mark.parametrize("shape", [(1, 1), (7, 13), (33, 257), (4096, 4096), (5, 1000)])
+def test_diag_matmul_shapes(shape, cuda_device):
+    from kbb200 import ops as K
+
+    a, b = torch.randn(shape[0]), torch.randn(shape)
+    got = K.diag_matmul(a.to(cuda_device), b.to(cuda_device)).cpu()
+    assert torch.equal(got, torch.diag(a) @ b) or torch.allclose(got, a[:, None] * b, atol=0, rtol=0)
