@@ -32,7 +32,10 @@
 //                generic -> async proxy, arrive on conv[s].
 //   warps 8-15   promotion + epilogue: tcgen05.ld each finished chunk, add
 //                into 128-lane x BN fp32 register totals (each warp owns one
-//                TMEM lane quarter and half the columns), store C at the end.
+//                TMEM lane quarter and half the columns); at the end stage
+//                the tile in shared memory (128B swizzle) and store it with
+//                TMA tensor stores (direct stores when C's strides do not
+//                allow a tensor map).
 // setmaxnreg moves registers from warpgroups 0-1 (64 each) to the promotion
 // warpgroups (192 each); the sum equals the 512 x 128 the CTA launches with.
 // Every mbarrier wait is bounded (%globaltimer); on expiry the CTA raises a
@@ -42,6 +45,7 @@
 // Shapes the TMA path cannot describe (row strides not multiples of 16 bytes,
 // unaligned bases) take a CUDA-core fp32 kernel.
 #include <cuda.h>
+#include <string.h>
 
 #include "kb_common.cuh"
 
@@ -131,6 +135,30 @@ __device__ __forceinline__ void tma_load_3d(uint32_t dst, const CUtensorMap* tm,
       "[%0], [%1, {%3, %4, %5}], [%2];" ::"r"(dst),
       "l"(reinterpret_cast<uint64_t>(tm)), "r"(bar), "r"(c0), "r"(c1), "r"(c2)
       : "memory");
+}
+__device__ __forceinline__ void tma_store_3d(const CUtensorMap* tm, uint32_t src, int c0, int c1, int c2) {
+  asm volatile(
+      "cp.async.bulk.tensor.3d.global.shared::cta.bulk_group [%0, {%2, %3, %4}], [%1];" ::"l"(
+          reinterpret_cast<uint64_t>(tm)),
+      "r"(src), "r"(c0), "r"(c1), "r"(c2)
+      : "memory");
+}
+__device__ __forceinline__ void bulk_commit_and_wait_read() {
+  asm volatile("cp.async.bulk.commit_group;" ::: "memory");
+  asm volatile("cp.async.bulk.wait_group.read 0;" ::: "memory");
+}
+// AND of `pred` over the `count` threads of named barrier `id` (also a barrier)
+__device__ __forceinline__ bool named_barrier_and(int id, int count, bool pred) {
+  uint32_t r;
+  asm volatile(
+      "{\n\t.reg .pred p, q;\n\t"
+      "setp.ne.u32 p, %1, 0;\n\t"
+      "barrier.red.and.pred q, %2, %3, p;\n\t"
+      "selp.u32 %0, 1, 0, q;\n\t}"
+      : "=r"(r)
+      : "r"((uint32_t)pred), "r"(id), "r"(count)
+      : "memory");
+  return r != 0;
 }
 __device__ __forceinline__ void fence_proxy_async() {
   asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
@@ -247,11 +275,13 @@ struct Params {
   int64_t batch_stride_c;
   int kb_per_split;  // mode 1: k-blocks per split
   int mode;          // 0: z = batch index, 1: z = split index (write partials)
+  int tma_store;     // 1: epilogue through shared memory + TMA tensor stores (tmC)
 };
 
 template <int BN, bool TRANS_A>
 __global__ void __launch_bounds__(kThreads, 1)
-gemm3x_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUtensorMap tmB, Params p) {
+gemm3x_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUtensorMap tmB,
+              const __grid_constant__ CUtensorMap tmC, Params p) {
   using CF = Cfg<BN>;
   constexpr int S = kStages;
   extern __shared__ uint8_t smem_raw[];
@@ -415,6 +445,32 @@ gemm3x_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ C
       tc_fence_before();
       mbar_arrive(chunk_empty(b));
     }
+    if (p.tma_store) {
+      // Stage the tile in the (now idle) stage buffers as BN/32 boxes of
+      // 128 rows x 128 B with the 128B swizzle (conflict-free writes), then
+      // one thread stores them with TMA; rows >= M / cols >= N are clipped.
+      const int r = q * 32 + lane;
+      if (ok) {
+#pragma unroll
+        for (int bx = 0; bx < NCOL / 32; ++bx) {
+          uint8_t* box = smem + (size_t)(col_base / 32 + bx) * (BM * 128);
+#pragma unroll
+          for (int c4 = 0; c4 < 8; ++c4)
+            *reinterpret_cast<float4*>(box + r * 128 + ((c4 ^ (r & 7)) * 16)) =
+                make_float4(tot[bx * 32 + c4 * 4], tot[bx * 32 + c4 * 4 + 1], tot[bx * 32 + c4 * 4 + 2],
+                            tot[bx * 32 + c4 * 4 + 3]);
+        }
+      }
+      fence_proxy_async();
+      const bool all_ok = named_barrier_and(1, kPromoThreads, ok);
+      if (pw == 0 && lane == 0 && all_ok) {
+        const int zc = p.mode == 1 ? z : batch;
+#pragma unroll 1
+        for (int bx = 0; bx < BN / 32; ++bx)
+          tma_store_3d(&tmC, smem_u32(smem + (size_t)bx * (BM * 128)), n0 + 32 * bx, m0, zc);
+        bulk_commit_and_wait_read();
+      }
+    } else {
     const int row = m0 + q * 32 + lane;
     float* out = p.C + (int64_t)batch * p.batch_stride_c;
     int64_t ldo = p.ldc;
@@ -435,6 +491,7 @@ gemm3x_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ C
         for (int j = 0; j < NCOL; ++j)
           if (col0 + j < p.N) orow[col0 + j] = tot[j];
       }
+    }
     }
   }
   tc_fence_before();
@@ -520,8 +577,26 @@ int make_map(CUtensorMap* tm, const float* base, int64_t inner, int64_t outer, i
   return KB_OK;
 }
 
+// 3-D fp32 tensor map for the C tile store: {N, M, Z} with box {32, 128, 1},
+// 128B swizzle (matches the staging layout of the epilogue).
+int make_store_map(CUtensorMap* tm, float* base, int64_t N, int64_t M, int64_t Z, int64_t row_stride,
+                   int64_t z_stride) {
+  EncodeFn enc = encode_fn();
+  KB_REQUIRE(enc != nullptr, KB_ERR_CUDA, "cuTensorMapEncodeTiled unavailable");
+  cuuint64_t dims[3] = {(cuuint64_t)N, (cuuint64_t)M, (cuuint64_t)Z};
+  cuuint64_t strides[2] = {(cuuint64_t)row_stride * 4, (cuuint64_t)z_stride * 4};
+  cuuint32_t box[3] = {32, (cuuint32_t)BM, 1};
+  cuuint32_t estr[3] = {1, 1, 1};
+  CUresult r = enc(tm, CU_TENSOR_MAP_DATA_TYPE_FLOAT32, 3, base, dims, strides, box, estr,
+                   CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B,
+                   CU_TENSOR_MAP_L2_PROMOTION_NONE, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+  KB_REQUIRE(r == CUDA_SUCCESS, KB_ERR_CUDA, "cuTensorMapEncodeTiled (C) failed (%d)", (int)r);
+  return KB_OK;
+}
+
 template <int BN, bool TA>
-int launch_tc(const CUtensorMap& ta, const CUtensorMap& tb, const Params& p, dim3 grid, cudaStream_t s) {
+int launch_tc(const CUtensorMap& ta, const CUtensorMap& tb, const CUtensorMap& tc, const Params& p, dim3 grid,
+              cudaStream_t s) {
   auto kern = gemm3x_kernel<BN, TA>;
   static uint64_t attr_set = 0;  // one bit per device ordinal
   int dev = 0;
@@ -530,7 +605,7 @@ int launch_tc(const CUtensorMap& ta, const CUtensorMap& tb, const Params& p, dim
     KB_CUDA(cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, Cfg<BN>::SMEM_BYTES));
     attr_set |= 1ull << dev;
   }
-  kern<<<grid, kThreads, Cfg<BN>::SMEM_BYTES, s>>>(ta, tb, p);
+  kern<<<grid, kThreads, Cfg<BN>::SMEM_BYTES, s>>>(ta, tb, tc, p);
   return check_launch("gemm3x_kernel");
 }
 
@@ -591,11 +666,24 @@ int run_gemm(const GemmArgs& g, int splits, float* ws, cudaStream_t s) {
     p.mode = 0;
     grid.z = (unsigned)g.batch;
   }
+  // TMA-store epilogue when C (or the partial buffer) is describable:
+  // 16-byte aligned base and row / batch strides that are multiples of 16 B
+  CUtensorMap tc;
+  memset(&tc, 0, sizeof(tc));
+  p.tma_store = 0;
+  if (p.mode == 1) {
+    if (aligned16(ws) && g.N % 4 == 0 &&
+        make_store_map(&tc, ws, g.N, g.M, grid.z, g.N, g.M * g.N) == KB_OK)
+      p.tma_store = 1;
+  } else if (aligned16(g.C) && g.ldc % 4 == 0 && (g.batch == 1 || g.sC % 4 == 0)) {
+    if (make_store_map(&tc, g.C, g.N, g.M, g.batch, g.ldc, g.batch > 1 ? g.sC : g.ldc * g.M) == KB_OK)
+      p.tma_store = 1;
+  }
   int st;
   if (bn256)
-    st = g.trans_a ? launch_tc<256, true>(ta, tb, p, grid, s) : launch_tc<256, false>(ta, tb, p, grid, s);
+    st = g.trans_a ? launch_tc<256, true>(ta, tb, tc, p, grid, s) : launch_tc<256, false>(ta, tb, tc, p, grid, s);
   else
-    st = g.trans_a ? launch_tc<128, true>(ta, tb, p, grid, s) : launch_tc<128, false>(ta, tb, p, grid, s);
+    st = g.trans_a ? launch_tc<128, true>(ta, tb, tc, p, grid, s) : launch_tc<128, false>(ta, tb, tc, p, grid, s);
   if (st) return st;
   if (splits > 1) {
     const int64_t total = g.M * g.N;
