@@ -1,19 +1,18 @@
 // gemv.cu — y[M] = A[M, K] x[K], fp32, HBM-bound (0.5 FLOP/byte).
 //
-// One 512-thread CTA per row: the row (4 MB at K = 2^20) is streamed once
-// with 128-bit evict-first loads, 4 float4 of A and 4 of x in flight per
+// One 256-thread CTA per row: the row (4 MB at K = 2^20) is streamed once
+// with 128-bit evict-first loads, 8 float4 of A and 8 of x in flight per
 // thread; x (4 MB) stays resident in the 126 MB L2 and is shared by every
 // CTA.  The row sum is a fixed shuffle tree, so y is deterministic (the
 // reference split rows into 32K chunks and combined them with fp32 atomics,
-// candidates/4_Matrix_vector_multiplication_/v1.py:16-33).  With 4 CTAs per
-// SM, 4096 rows are ~7 full waves over 148 SMs.
+// candidates/4_Matrix_vector_multiplication_/v1.py:16-33).
 #include "kb_common.cuh"
 
 namespace kb {
 namespace {
 
-constexpr int kThreads = 512;
-constexpr int kUnroll = 4;
+constexpr int kThreads = 256;
+constexpr int kUnroll = 8;
 
 __global__ void __launch_bounds__(kThreads)
 gemv_vec4_kernel(const float* __restrict__ A, const float* __restrict__ x,
@@ -23,7 +22,9 @@ gemv_vec4_kernel(const float* __restrict__ A, const float* __restrict__ x,
   const float4* a4 = reinterpret_cast<const float4*>(A + row * K);
   const float4* x4 = reinterpret_cast<const float4*>(x);
   const int64_t nvec = K / 4;
-  float acc[kUnroll] = {0.f, 0.f, 0.f, 0.f};
+  float acc[kUnroll];
+#pragma unroll
+  for (int u = 0; u < kUnroll; ++u) acc[u] = 0.f;
   int64_t i = threadIdx.x;
   const int64_t step = (int64_t)kThreads * kUnroll;
   for (; i + (kUnroll - 1) * kThreads < nvec; i += step) {
@@ -41,7 +42,9 @@ gemv_vec4_kernel(const float* __restrict__ A, const float* __restrict__ x,
     const float4 a = ld_stream(a4 + i), b = __ldg(x4 + i);
     acc[0] = fmaf(a.x, b.x, fmaf(a.y, b.y, fmaf(a.z, b.z, fmaf(a.w, b.w, acc[0]))));
   }
-  float s = (acc[0] + acc[1]) + (acc[2] + acc[3]);
+  float s = 0.f;
+#pragma unroll
+  for (int u = 0; u < kUnroll; ++u) s += acc[u];
   for (int64_t j = nvec * 4 + threadIdx.x; j < K; j += kThreads) s = fmaf(A[row * K + j], x[j], s);
   s = block_sum<kThreads>(s, red);
   if (threadIdx.x == 0) y[row] = s;
