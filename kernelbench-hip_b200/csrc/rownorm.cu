@@ -45,15 +45,56 @@ struct RowArgs {
 // ---------------------------------------------------------------------------
 // reducers: warp-only, block, and block + cluster (DSMEM)
 // ---------------------------------------------------------------------------
+// Partial softmax statistics: max m and sum of exp(x - m).  Two partials
+// combine as (M, s1 e^(m1 - M) + s2 e^(m2 - M)), M = max(m1, m2); the
+// combination is commutative, so butterfly shuffles leave every lane with
+// the same bits.  A NaN element makes its sum NaN, which then propagates.
+struct MaxSum {
+  float m, s;
+};
+__device__ __forceinline__ float ms_rescale(float m, float M) {
+  return m == M ? 1.0f : exp2f((m - M) * kLog2e);  // also covers m == M == -inf
+}
+__device__ __forceinline__ MaxSum ms_combine(MaxSum a, MaxSum b) {
+  const float M = fmaxf(a.m, b.m);
+  return {M, a.s * ms_rescale(a.m, M) + b.s * ms_rescale(b.m, M)};
+}
+__device__ __forceinline__ MaxSum warp_ms(MaxSum v) {
+#pragma unroll
+  for (int o = 16; o > 0; o >>= 1) {
+    const MaxSum u{__shfl_xor_sync(0xffffffffu, v.m, o), __shfl_xor_sync(0xffffffffu, v.s, o)};
+    v = ms_combine(v, u);
+  }
+  return v;
+}
+// Block-wide combine; `red` holds >= 64 floats.
+template <int NT>
+__device__ __forceinline__ MaxSum block_ms(MaxSum v, float* red) {
+  constexpr int NW = NT / 32;
+  const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
+  v = warp_ms(v);
+  if (NW == 1) return v;
+  if (lane == 0) {
+    red[warp] = v.m;
+    red[32 + warp] = v.s;
+  }
+  __syncthreads();
+  MaxSum r = (lane < NW) ? MaxSum{red[lane], red[32 + lane]} : MaxSum{-INFINITY, 0.0f};
+  r = warp_ms(r);
+  __syncthreads();
+  return r;
+}
+
 struct WarpReducer {
   __device__ __forceinline__ float sum(float v, int) const { return warp_sum(v); }
   __device__ __forceinline__ float max(float v, int) const { return warp_max(v); }
+  __device__ __forceinline__ MaxSum maxsum(MaxSum v, int) const { return warp_ms(v); }
 };
 
 template <int NT, int CL>
 struct ClusterReducer {
-  float* red;    // >= 32 floats of shared memory
-  float* slots;  // >= 2 floats of shared memory, one per reduction stage
+  float* red;    // >= 64 floats of shared memory
+  float* slots;  // >= 4 floats of shared memory: reduction stages 0 and 1
   __device__ __forceinline__ float combine_sum(float part, int slot) const {
     if constexpr (CL == 1) {
       return part;
@@ -85,6 +126,26 @@ struct ClusterReducer {
   }
   __device__ __forceinline__ float max(float v, int slot) const {
     return combine_max(block_max<NT>(v, red), slot);
+  }
+  __device__ __forceinline__ MaxSum maxsum(MaxSum v, int slot) const {
+    MaxSum part = block_ms<NT>(v, red);
+    if constexpr (CL == 1) {
+      return part;
+    } else {
+      cg::cluster_group cluster = cg::this_cluster();
+      if (threadIdx.x == 0) {
+        slots[2 * slot] = part.m;
+        slots[2 * slot + 1] = part.s;
+      }
+      cluster.sync();
+      MaxSum tot{-INFINITY, 0.0f};
+#pragma unroll
+      for (int r = 0; r < CL; ++r) {
+        const float* rs = cluster.map_shared_rank(slots + 2 * slot, r);
+        tot = ms_combine(tot, MaxSum{rs[0], rs[1]});
+      }
+      return tot;
+    }
   }
 };
 
@@ -158,39 +219,42 @@ __device__ __forceinline__ void row_math(float4 (&v)[VPT], const bool (&ok)[VPT]
         st_stream(yrow + (int64_t)k * stride + lane, r);
       }
   } else {
-    float m = -INFINITY;
+    // one pass: this thread's max and sum of exp(x - max), then a single
+    // block (cluster) combine of the (max, sum) pairs
+    float mt = -INFINITY;
 #pragma unroll
     for (int k = 0; k < VPT; ++k)
-      if (ok[k]) m = fmaxf(m, fmaxf(fmaxf(v[k].x, v[k].y), fmaxf(v[k].z, v[k].w)));
-    m = red.max(m, 0);
-    // exp(x - m) = 2^(x log2(e) - m log2(e)): one FMA and exp2f per element
-    const float ml = (m == -INFINITY) ? 0.0f : m * kLog2e;
-    float s = 0.0f;
+      if (ok[k]) mt = fmaxf(mt, fmaxf(fmaxf(v[k].x, v[k].y), fmaxf(v[k].z, v[k].w)));
+    // exp(x - mt) = 2^(x log2(e) - mt log2(e)): one FMA and exp2f per element
+    const float mtl = (mt == -INFINITY) ? 0.0f : mt * kLog2e;
+    float st = 0.0f;
     if constexpr (OP == kSoftmax) {
-      // keep exp(x - m) in registers: exp is evaluated once per element
+      // keep exp(x - mt) in registers: exp is evaluated once per element
 #pragma unroll
       for (int k = 0; k < VPT; ++k)
         if (ok[k]) {
-          v[k].x = exp2f(fmaf(v[k].x, kLog2e, -ml));
-          v[k].y = exp2f(fmaf(v[k].y, kLog2e, -ml));
-          v[k].z = exp2f(fmaf(v[k].z, kLog2e, -ml));
-          v[k].w = exp2f(fmaf(v[k].w, kLog2e, -ml));
-          s += (v[k].x + v[k].y) + (v[k].z + v[k].w);
+          v[k].x = exp2f(fmaf(v[k].x, kLog2e, -mtl));
+          v[k].y = exp2f(fmaf(v[k].y, kLog2e, -mtl));
+          v[k].z = exp2f(fmaf(v[k].z, kLog2e, -mtl));
+          v[k].w = exp2f(fmaf(v[k].w, kLog2e, -mtl));
+          st += (v[k].x + v[k].y) + (v[k].z + v[k].w);
         }
-      const float inv = 1.0f / red.sum(s, 1);
+      const MaxSum tot = red.maxsum(MaxSum{mt, st}, 0);
+      const float scale = ms_rescale(mt, tot.m) / tot.s;
 #pragma unroll
       for (int k = 0; k < VPT; ++k)
         if (ok[k] && store) {
-          float4 r = make_float4(v[k].x * inv, v[k].y * inv, v[k].z * inv, v[k].w * inv);
+          float4 r = make_float4(v[k].x * scale, v[k].y * scale, v[k].z * scale, v[k].w * scale);
           st_stream(yrow + (int64_t)k * stride + lane, r);
         }
     } else {
 #pragma unroll
       for (int k = 0; k < VPT; ++k)
         if (ok[k])
-          s += (exp2f(fmaf(v[k].x, kLog2e, -ml)) + exp2f(fmaf(v[k].y, kLog2e, -ml))) +
-               (exp2f(fmaf(v[k].z, kLog2e, -ml)) + exp2f(fmaf(v[k].w, kLog2e, -ml)));
-      const float lse = logf(red.sum(s, 1));
+          st += (exp2f(fmaf(v[k].x, kLog2e, -mtl)) + exp2f(fmaf(v[k].y, kLog2e, -mtl))) +
+                (exp2f(fmaf(v[k].z, kLog2e, -mtl)) + exp2f(fmaf(v[k].w, kLog2e, -mtl)));
+      const MaxSum tot = red.maxsum(MaxSum{mt, st}, 0);
+      const float m = tot.m, lse = logf(tot.s);
 #pragma unroll
       for (int k = 0; k < VPT; ++k)
         if (ok[k] && store) {
@@ -205,8 +269,8 @@ __device__ __forceinline__ void row_math(float4 (&v)[VPT], const bool (&ok)[VPT]
 // One CTA (or one CL-CTA cluster) per row; NT threads x VPT float4 each.
 template <RowOp OP, int NT, int VPT, int CL>
 __global__ void __launch_bounds__(NT) row_block_kernel(RowArgs a) {
-  __shared__ float red[32];
-  __shared__ float slots[2];
+  __shared__ float red[64];
+  __shared__ float slots[4];
   const int64_t row = blockIdx.x / CL;
   int rank = 0;
   if constexpr (CL > 1) rank = (int)cg::this_cluster().block_rank();
@@ -284,8 +348,8 @@ __device__ __forceinline__ void bulk_load(uint32_t dst, const void* src, uint32_
 template <RowOp OP, int NT, int VPT, int CL, int DEPTH>
 __global__ void __launch_bounds__(NT) row_persist_kernel(RowArgs a) {
   extern __shared__ float4 seg_buf[];  // DEPTH segment buffers
-  __shared__ float red[32];
-  __shared__ float slots[2];
+  __shared__ float red[64];
+  __shared__ float slots[4];
   __shared__ __align__(8) uint64_t bars[DEPTH];
   int rank = 0;
   if constexpr (CL > 1) rank = (int)cg::this_cluster().block_rank();
