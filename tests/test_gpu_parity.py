@@ -74,6 +74,19 @@ def test_elementwise_unaligned_view(op, cuda_device):
     assert_close(y.cpu().numpy(), getattr(O, op)(x.cpu().numpy()), EXACT if op == "relu" else 1e-5)
 
 
+@pytest.mark.parametrize("op", ["gelu_erf", "relu"])
+def test_elementwise_16b_aligned_view(op, cuda_device):
+    """16-byte but not 32-byte aligned views take the 128-bit tile path."""
+    from kbb200 import ops as K
+
+    base = torch.randn(3 * 4096 + 4 + 100, device=cuda_device) * 4
+    x = base[4:]
+    y = torch.empty(base.numel(), device=cuda_device)[4:]
+    assert x.data_ptr() % 32 == 16 and y.data_ptr() % 32 == 16
+    getattr(K, op)(x, out=y)
+    assert_close(y.cpu().numpy(), getattr(O, op)(x.cpu().numpy()), EXACT if op == "relu" else 1e-5)
+
+
 def test_relu_special_values(cuda_device):
     from kbb200 import ops as K
 
@@ -419,7 +432,7 @@ def test_gemm_accuracy_matches_fp32_cublas(mnk, cuda_device):
     assert e_ours <= 4 * e_torch + 1e-6, f"3xTF32 max error {e_ours:.3e} vs fp32 {e_torch:.3e}"
 
 
-@pytest.mark.parametrize("shape", [(1, 1), (7, 13), (33, 257), (4096, 4096), (5, 1000)])
+@pytest.mark.parametrize("shape", [(1, 1), (7, 13), (33, 257), (4096, 4096), (5, 1000), (64, 1028), (96, 4100)])
 def test_diag_matmul_shapes(shape, cuda_device):
     from kbb200 import ops as K
 
