@@ -19,7 +19,12 @@
 // error then scales with the magnitude of one chunk, not of the whole sum,
 // and stays at the level of an fp32 CUDA-core GEMM.
 //
-// CTA = one 128 x BN output tile, 512 threads in 4 warpgroups:
+// Persistent CTAs, one per SM, walk the 128 x BN output tiles in order
+// (tile id = blockIdx.x, + gridDim.x, ...).  Every role keeps running
+// counters across tiles, so the stage ring and the two TMEM chunk buffers
+// simply continue: while the promotion warps store tile t, the MMA warp is
+// already accumulating tile t + 1 into the other buffer.
+// CTA = 512 threads in 4 warpgroups:
 //   warp 0       TMA producer: cp.async.bulk.tensor loads of the A tile
 //                (128 x 16, K-major, 64B swizzle) and B tile (16 x BN,
 //                N-major, 32-column boxes, 128B swizzle with 32-byte atoms)
@@ -32,10 +37,11 @@
 //                generic -> async proxy, arrive on conv[s].
 //   warps 8-15   promotion + epilogue: tcgen05.ld each finished chunk, add
 //                into 128-lane x BN fp32 register totals (each warp owns one
-//                TMEM lane quarter and half the columns); at the end stage
-//                the tile in shared memory (128B swizzle) and store it with
-//                TMA tensor stores (direct stores when C's strides do not
-//                allow a tensor map).
+//                TMEM lane quarter and half the columns); at the end of a
+//                tile each warp stages its 32-row x 32-column boxes in its
+//                own 4 KB buffer (128B swizzle) and stores them with TMA
+//                tensor stores (direct stores when C's strides do not allow
+//                a tensor map).
 // setmaxnreg moves registers from warpgroups 0-1 (64 each) to the promotion
 // warpgroups (192 each); the sum equals the 512 x 128 the CTA launches with.
 // Every mbarrier wait is bounded (%globaltimer); on expiry the CTA raises a
@@ -66,14 +72,18 @@ constexpr int kConvThreads = kConvWarps * 32;
 constexpr int kPromoWarp0 = 8, kPromoWarps = 8;
 constexpr int kPromoThreads = kPromoWarps * 32;
 constexpr uint64_t kWaitLimitNs = 2000000000ull;
+constexpr int kBoxRows = 32, kBoxCols = 32;      // C store box: 32 rows x 128 B
+constexpr int kBoxBytes = kBoxRows * kBoxCols * 4;
 
 template <int BN>
 struct Cfg {
   static constexpr int A_BYTES = BM * BK * 4;                  // 8 KB
   static constexpr int B_BYTES = BN * BK * 4;                  // 16 KB (BN 256)
   static constexpr int STAGE_BYTES = 2 * (A_BYTES + B_BYTES);  // raw + lo buffers
+  static constexpr int STAGING_BYTES = kPromoWarps * kBoxBytes;  // one C box per promotion warp
   static constexpr int BAR_BYTES = 256;
-  static constexpr int SMEM_BYTES = kStages * STAGE_BYTES + BAR_BYTES + 1024;  // + alignment slack
+  static constexpr int SMEM_BYTES =
+      kStages * STAGE_BYTES + STAGING_BYTES + BAR_BYTES + 1024;  // + alignment slack
   static constexpr int TMEM_COLS = 2 * BN;                     // two chunk accumulators
   static constexpr int COLS_PER_WARP = BN / 2;                 // promotion warps split columns
 };
@@ -143,23 +153,11 @@ __device__ __forceinline__ void tma_store_3d(const CUtensorMap* tm, uint32_t src
       "r"(src), "r"(c0), "r"(c1), "r"(c2)
       : "memory");
 }
-__device__ __forceinline__ void bulk_commit_and_wait_read() {
-  asm volatile("cp.async.bulk.commit_group;" ::: "memory");
+__device__ __forceinline__ void bulk_commit() { asm volatile("cp.async.bulk.commit_group;" ::: "memory"); }
+__device__ __forceinline__ void bulk_wait_read_all() {
   asm volatile("cp.async.bulk.wait_group.read 0;" ::: "memory");
 }
-// AND of `pred` over the `count` threads of named barrier `id` (also a barrier)
-__device__ __forceinline__ bool named_barrier_and(int id, int count, bool pred) {
-  uint32_t r;
-  asm volatile(
-      "{\n\t.reg .pred p, q;\n\t"
-      "setp.ne.u32 p, %1, 0;\n\t"
-      "barrier.red.and.pred q, %2, %3, p;\n\t"
-      "selp.u32 %0, 1, 0, q;\n\t}"
-      : "=r"(r)
-      : "r"((uint32_t)pred), "r"(id), "r"(count)
-      : "memory");
-  return r != 0;
-}
+__device__ __forceinline__ void bulk_wait_all() { asm volatile("cp.async.bulk.wait_group 0;" ::: "memory"); }
 __device__ __forceinline__ void fence_proxy_async() {
   asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
 }
@@ -276,7 +274,30 @@ struct Params {
   int kb_per_split;  // mode 1: k-blocks per split
   int mode;          // 0: z = batch index, 1: z = split index (write partials)
   int tma_store;     // 1: epilogue through shared memory + TMA tensor stores (tmC)
+  int tiles_n, tiles_m, tiles_z;  // output tile grid, n fastest
 };
+
+// One output tile: its corner, batch / split index and k-block range.
+struct Tile {
+  int n0, m0, z, batch, kb_begin, nk;
+};
+__device__ __forceinline__ Tile tile_at(const Params& p, int t, int bn, int nk_total) {
+  Tile T;
+  const int rest = t / p.tiles_n;
+  T.n0 = (t - rest * p.tiles_n) * bn;
+  T.m0 = (rest % p.tiles_m) * BM;
+  T.z = rest / p.tiles_m;
+  T.batch = T.z;
+  T.kb_begin = 0;
+  int kb_end = nk_total;
+  if (p.mode == 1) {  // z is the split index
+    T.kb_begin = T.z * p.kb_per_split;
+    kb_end = min(nk_total, T.kb_begin + p.kb_per_split);
+    T.batch = 0;
+  }
+  T.nk = max(kb_end - T.kb_begin, 0);
+  return T;
+}
 
 template <int BN, bool TRANS_A>
 __global__ void __launch_bounds__(kThreads, 1)
@@ -286,23 +307,15 @@ gemm3x_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ C
   constexpr int S = kStages;
   extern __shared__ uint8_t smem_raw[];
   uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
-  uint64_t* bars = reinterpret_cast<uint64_t*>(smem + S * CF::STAGE_BYTES);
+  uint8_t* staging = smem + S * CF::STAGE_BYTES;  // 1024-aligned: STAGE_BYTES is a multiple of 1 KB
+  uint64_t* bars = reinterpret_cast<uint64_t*>(staging + CF::STAGING_BYTES);
   // bars: [0,S) full, [S,2S) conv, [2S,3S) empty, [3S,3S+2) chunk_full, [3S+2,3S+4) chunk_empty
   uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(bars + 3 * S + 4);
   volatile int* abort_flag = reinterpret_cast<volatile int*>(tmem_slot + 1);
 
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
-  const int n0 = blockIdx.x * BN, m0 = blockIdx.y * BM;
-  const int z = blockIdx.z;
   const int nk_total = (p.K + BK - 1) / BK;
-  int kb_begin = 0, kb_end = nk_total, batch = z;
-  if (p.mode == 1) {
-    kb_begin = z * p.kb_per_split;
-    kb_end = min(nk_total, kb_begin + p.kb_per_split);
-    batch = 0;
-  }
-  const int nk = max(kb_end - kb_begin, 0);
-  const int nchunks = (nk + kChunkBlocks - 1) / kChunkBlocks;
+  const int ntiles = p.tiles_n * p.tiles_m * p.tiles_z;
 
   auto full = [&](int s) { return smem_u32(bars + s); };
   auto conv = [&](int s) { return smem_u32(bars + S + s); };
@@ -334,35 +347,44 @@ gemm3x_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ C
 
   auto stage_ptr = [&](int s) { return smem + s * CF::STAGE_BYTES; };
 
+  // Every role walks the same tiles; g counts k-blocks (stage ring slots)
+  // and gc TMEM chunks over all tiles of this CTA.
   if (warp < kPromoWarp0) {
     setmaxnreg_dec64();
     if (warp == 0) {
       // ---------------- TMA producer
       if (lane == 0) {
-        int issued = 0;
-        for (int it = 0; it < nk; ++it) {
-          const int s = it % S;
-          if (!mbar_wait(empty(s), ((it / S) & 1) ^ 1, abort_flag)) break;
-          uint8_t* st = stage_ptr(s);
-          const int k0 = (kb_begin + it) * BK;
-          mbar_expect_tx(full(s), CF::A_BYTES + CF::B_BYTES);
-          if (TRANS_A) {
+        int g = 0;
+        bool alive = true;
+        for (int t = blockIdx.x; t < ntiles && alive; t += gridDim.x) {
+          const Tile T = tile_at(p, t, BN, nk_total);
+          for (int it = 0; it < T.nk; ++it) {
+            const int s = g % S;
+            if (!mbar_wait(empty(s), ((g / S) & 1) ^ 1, abort_flag)) {
+              alive = false;
+              break;
+            }
+            uint8_t* st = stage_ptr(s);
+            const int k0 = (T.kb_begin + it) * BK;
+            mbar_expect_tx(full(s), CF::A_BYTES + CF::B_BYTES);
+            if (TRANS_A) {
 #pragma unroll
-            for (int j = 0; j < BM / 32; ++j)
-              tma_load_3d(smem_u32(st + j * 2048), &tmA, full(s), m0 + 32 * j, k0, batch);
-          } else {
-            tma_load_3d(smem_u32(st), &tmA, full(s), k0, m0, batch);
+              for (int j = 0; j < BM / 32; ++j)
+                tma_load_3d(smem_u32(st + j * 2048), &tmA, full(s), T.m0 + 32 * j, k0, T.batch);
+            } else {
+              tma_load_3d(smem_u32(st), &tmA, full(s), k0, T.m0, T.batch);
+            }
+#pragma unroll
+            for (int j = 0; j < BN / 32; ++j)
+              tma_load_3d(smem_u32(st + CF::A_BYTES + j * 2048), &tmB, full(s), T.n0 + 32 * j, k0, T.batch);
+            ++g;
           }
-#pragma unroll
-          for (int j = 0; j < BN / 32; ++j)
-            tma_load_3d(smem_u32(st + CF::A_BYTES + j * 2048), &tmB, full(s), n0 + 32 * j, k0, batch);
-          ++issued;
         }
         // drain: every issued load must land before the CTA may exit
-        for (int it = max(issued - S, 0); it < issued; ++it) {
-          const int s = it % S;
+        for (int gi = max(g - S, 0); gi < g; ++gi) {
+          const int s = gi % S;
           const uint64_t t0 = globaltimer();
-          while (!mbar_try_wait(full(s), (it / S) & 1)) {
+          while (!mbar_try_wait(full(s), (gi / S) & 1)) {
             if (globaltimer() - t0 > kWaitLimitNs) break;
           }
         }
@@ -371,50 +393,71 @@ gemm3x_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ C
       // ---------------- MMA issuer
       if (lane == 0) {
         constexpr uint32_t idesc = make_idesc(BM, BN, TRANS_A);
+        int g = 0, gc = 0;
         bool alive = true;
-        for (int it = 0; it < nk && alive; ++it) {
-          const int s = it % S;
-          const int c = it / kChunkBlocks, b = c & 1;
-          const bool chunk_first = (it % kChunkBlocks) == 0;
-          const bool chunk_last = (it % kChunkBlocks) == kChunkBlocks - 1 || it == nk - 1;
-          if (chunk_first && !mbar_wait(chunk_empty(b), ((c >> 1) & 1) ^ 1, abort_flag)) break;
-          if (!mbar_wait(conv(s), (it / S) & 1, abort_flag)) break;
-          tc_fence_after();
-          uint8_t* st = stage_ptr(s);
-          const uint32_t a_hi = smem_u32(st);
-          const uint32_t b_hi = a_hi + CF::A_BYTES;
-          const uint32_t a_lo = b_hi + CF::B_BYTES;
-          const uint32_t b_lo = a_lo + CF::A_BYTES;
-          const uint32_t d = tmem + (uint32_t)(b * BN);
+        for (int t = blockIdx.x; t < ntiles && alive; t += gridDim.x) {
+          const Tile T = tile_at(p, t, BN, nk_total);
+          for (int it = 0; it < T.nk; ++it, ++g) {
+            const int s = g % S;
+            const int b = gc & 1;
+            const bool chunk_first = (it % kChunkBlocks) == 0;
+            const bool chunk_last = (it % kChunkBlocks) == kChunkBlocks - 1 || it == T.nk - 1;
+            if (chunk_first && !mbar_wait(chunk_empty(b), ((gc >> 1) & 1) ^ 1, abort_flag)) {
+              alive = false;
+              break;
+            }
+            if (!mbar_wait(conv(s), (g / S) & 1, abort_flag)) {
+              alive = false;
+              break;
+            }
+            tc_fence_after();
+            uint8_t* st = stage_ptr(s);
+            const uint32_t a_hi = smem_u32(st);
+            const uint32_t b_hi = a_hi + CF::A_BYTES;
+            const uint32_t a_lo = b_hi + CF::B_BYTES;
+            const uint32_t b_lo = a_lo + CF::A_BYTES;
+            const uint32_t d = tmem + (uint32_t)(b * BN);
 #pragma unroll
-          for (int kk = 0; kk < BK / 8; ++kk) {
-            const uint32_t aoff = TRANS_A ? kk * 1024 : kk * 32;
-            const uint32_t boff = kk * 1024;
-            const uint64_t dah = TRANS_A ? desc_mnmajor(a_hi + aoff) : desc_kmajor(a_hi + aoff);
-            const uint64_t dal = TRANS_A ? desc_mnmajor(a_lo + aoff) : desc_kmajor(a_lo + aoff);
-            const uint64_t dbh = desc_mnmajor(b_hi + boff);
-            const uint64_t dbl = desc_mnmajor(b_lo + boff);
-            mma_tf32(d, dal, dbh, idesc, (chunk_first && kk == 0) ? 0u : 1u);
-            mma_tf32(d, dah, dbl, idesc, 1u);
-            mma_tf32(d, dah, dbh, idesc, 1u);
+            for (int kk = 0; kk < BK / 8; ++kk) {
+              const uint32_t aoff = TRANS_A ? kk * 1024 : kk * 32;
+              const uint32_t boff = kk * 1024;
+              const uint64_t dah = TRANS_A ? desc_mnmajor(a_hi + aoff) : desc_kmajor(a_hi + aoff);
+              const uint64_t dal = TRANS_A ? desc_mnmajor(a_lo + aoff) : desc_kmajor(a_lo + aoff);
+              const uint64_t dbh = desc_mnmajor(b_hi + boff);
+              const uint64_t dbl = desc_mnmajor(b_lo + boff);
+              mma_tf32(d, dal, dbh, idesc, (chunk_first && kk == 0) ? 0u : 1u);
+              mma_tf32(d, dah, dbl, idesc, 1u);
+              mma_tf32(d, dah, dbh, idesc, 1u);
+            }
+            mma_commit(empty(s));
+            if (chunk_last) {
+              mma_commit(chunk_full(b));
+              ++gc;
+            }
           }
-          mma_commit(empty(s));
-          if (chunk_last) mma_commit(chunk_full(b));
         }
       }
     } else {
       // ---------------- lo converters (warps 2..7)
-      const int t = threadIdx.x - kConvWarp0 * 32;
-      for (int it = 0; it < nk; ++it) {
-        const int s = it % S;
-        if (!mbar_wait(full(s), (it / S) & 1, abort_flag)) break;
-        uint8_t* st = stage_ptr(s);
-        lo_buffer(reinterpret_cast<const float4*>(st),
-                  reinterpret_cast<float4*>(st + CF::A_BYTES + CF::B_BYTES), CF::A_BYTES / 16, t);
-        lo_buffer(reinterpret_cast<const float4*>(st + CF::A_BYTES),
-                  reinterpret_cast<float4*>(st + 2 * CF::A_BYTES + CF::B_BYTES), CF::B_BYTES / 16, t);
-        fence_proxy_async();
-        mbar_arrive(conv(s));
+      const int t0 = threadIdx.x - kConvWarp0 * 32;
+      int g = 0;
+      bool alive = true;
+      for (int t = blockIdx.x; t < ntiles && alive; t += gridDim.x) {
+        const Tile T = tile_at(p, t, BN, nk_total);
+        for (int it = 0; it < T.nk; ++it, ++g) {
+          const int s = g % S;
+          if (!mbar_wait(full(s), (g / S) & 1, abort_flag)) {
+            alive = false;
+            break;
+          }
+          uint8_t* st = stage_ptr(s);
+          lo_buffer(reinterpret_cast<const float4*>(st),
+                    reinterpret_cast<float4*>(st + CF::A_BYTES + CF::B_BYTES), CF::A_BYTES / 16, t0);
+          lo_buffer(reinterpret_cast<const float4*>(st + CF::A_BYTES),
+                    reinterpret_cast<float4*>(st + 2 * CF::A_BYTES + CF::B_BYTES), CF::B_BYTES / 16, t0);
+          fence_proxy_async();
+          mbar_arrive(conv(s));
+        }
       }
     }
   } else {
@@ -424,75 +467,79 @@ gemm3x_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ C
     const int q = warp & 3;                         // TMEM lane quarter this warp may access
     const int col_base = (pw >> 2) * CF::COLS_PER_WARP;
     constexpr int NCOL = CF::COLS_PER_WARP;
-    float tot[NCOL];
-#pragma unroll
-    for (int j = 0; j < NCOL; ++j) tot[j] = 0.0f;
+    uint8_t* box = staging + pw * kBoxBytes;        // this warp's 32 x 32 C box
+    int gc = 0;
     bool ok = true;
-    for (int c = 0; c < nchunks; ++c) {
-      const int b = c & 1;
-      ok = __all_sync(0xffffffffu, mbar_wait(chunk_full(b), (c >> 1) & 1, abort_flag));
-      if (!ok) break;
-      tc_fence_after();
-      const uint32_t base = tmem + ((uint32_t)(q * 32) << 16) + (uint32_t)(b * BN + col_base);
+    for (int t = blockIdx.x; t < ntiles && ok; t += gridDim.x) {
+      const Tile T = tile_at(p, t, BN, nk_total);
+      const int nchunks = (T.nk + kChunkBlocks - 1) / kChunkBlocks;
+      float tot[NCOL];
 #pragma unroll
-      for (int j = 0; j < NCOL / 32; ++j) {
-        uint32_t r[32];
-        tmem_ld32(base + j * 32, r);
-        tmem_ld_wait();
+      for (int j = 0; j < NCOL; ++j) tot[j] = 0.0f;
+      for (int c = 0; c < nchunks; ++c, ++gc) {
+        const int b = gc & 1;
+        ok = __all_sync(0xffffffffu, mbar_wait(chunk_full(b), (gc >> 1) & 1, abort_flag));
+        if (!ok) break;
+        tc_fence_after();
+        const uint32_t base = tmem + ((uint32_t)(q * 32) << 16) + (uint32_t)(b * BN + col_base);
 #pragma unroll
-        for (int i = 0; i < 32; ++i) tot[j * 32 + i] += __uint_as_float(r[i]);
+        for (int j = 0; j < NCOL / 32; ++j) {
+          uint32_t r[32];
+          tmem_ld32(base + j * 32, r);
+          tmem_ld_wait();
+#pragma unroll
+          for (int i = 0; i < 32; ++i) tot[j * 32 + i] += __uint_as_float(r[i]);
+        }
+        tc_fence_before();
+        mbar_arrive(chunk_empty(b));
       }
-      tc_fence_before();
-      mbar_arrive(chunk_empty(b));
-    }
-    if (p.tma_store) {
-      // Stage the tile in the (now idle) stage buffers as BN/32 boxes of
-      // 128 rows x 128 B with the 128B swizzle (conflict-free writes), then
-      // one thread stores them with TMA; rows >= M / cols >= N are clipped.
-      const int r = q * 32 + lane;
-      if (ok) {
+      if (!ok) break;
+      if (p.tma_store) {
+        // Rows q*32 + lane of the tile, 32 columns per box, 128B swizzle
+        // (conflict-free writes).  The box buffer is reused once the previous
+        // store from it has been read; rows >= M / cols >= N are clipped.
+        const int zc = p.mode == 1 ? T.z : T.batch;
 #pragma unroll
         for (int bx = 0; bx < NCOL / 32; ++bx) {
-          uint8_t* box = smem + (size_t)(col_base / 32 + bx) * (BM * 128);
+          if (lane == 0) bulk_wait_read_all();
+          __syncwarp();
 #pragma unroll
           for (int c4 = 0; c4 < 8; ++c4)
-            *reinterpret_cast<float4*>(box + r * 128 + ((c4 ^ (r & 7)) * 16)) =
+            *reinterpret_cast<float4*>(box + lane * 128 + ((c4 ^ (lane & 7)) * 16)) =
                 make_float4(tot[bx * 32 + c4 * 4], tot[bx * 32 + c4 * 4 + 1], tot[bx * 32 + c4 * 4 + 2],
                             tot[bx * 32 + c4 * 4 + 3]);
+          fence_proxy_async();
+          __syncwarp();
+          if (lane == 0) {
+            tma_store_3d(&tmC, smem_u32(box), T.n0 + col_base + 32 * bx, T.m0 + q * 32, zc);
+            bulk_commit();
+          }
+        }
+      } else {
+        const int row = T.m0 + q * 32 + lane;
+        float* out = p.C + (int64_t)T.batch * p.batch_stride_c;
+        int64_t ldo = p.ldc;
+        if (p.mode == 1) {
+          out = p.C + (int64_t)T.z * p.M * p.N;
+          ldo = p.N;
+        }
+        if (row < p.M) {
+          float* orow = out + (int64_t)row * ldo;
+          const int col0 = T.n0 + col_base;
+          const bool vec = ((ldo & 3) == 0) && ((reinterpret_cast<uintptr_t>(out) & 15) == 0);
+          if (vec && col0 + NCOL <= p.N) {
+#pragma unroll
+            for (int j = 0; j < NCOL; j += 4)
+              *reinterpret_cast<float4*>(orow + col0 + j) = make_float4(tot[j], tot[j + 1], tot[j + 2], tot[j + 3]);
+          } else {
+#pragma unroll
+            for (int j = 0; j < NCOL; ++j)
+              if (col0 + j < p.N) orow[col0 + j] = tot[j];
+          }
         }
       }
-      fence_proxy_async();
-      const bool all_ok = named_barrier_and(1, kPromoThreads, ok);
-      if (pw == 0 && lane == 0 && all_ok) {
-        const int zc = p.mode == 1 ? z : batch;
-#pragma unroll 1
-        for (int bx = 0; bx < BN / 32; ++bx)
-          tma_store_3d(&tmC, smem_u32(smem + (size_t)bx * (BM * 128)), n0 + 32 * bx, m0, zc);
-        bulk_commit_and_wait_read();
-      }
-    } else {
-    const int row = m0 + q * 32 + lane;
-    float* out = p.C + (int64_t)batch * p.batch_stride_c;
-    int64_t ldo = p.ldc;
-    if (p.mode == 1) {
-      out = p.C + (int64_t)z * p.M * p.N;
-      ldo = p.N;
     }
-    if (ok && row < p.M) {
-      float* orow = out + (int64_t)row * ldo;
-      const int col0 = n0 + col_base;
-      const bool vec = ((ldo & 3) == 0) && ((reinterpret_cast<uintptr_t>(out) & 15) == 0);
-      if (vec && col0 + NCOL <= p.N) {
-#pragma unroll
-        for (int j = 0; j < NCOL; j += 4)
-          *reinterpret_cast<float4*>(orow + col0 + j) = make_float4(tot[j], tot[j + 1], tot[j + 2], tot[j + 3]);
-      } else {
-#pragma unroll
-        for (int j = 0; j < NCOL; ++j)
-          if (col0 + j < p.N) orow[col0 + j] = tot[j];
-      }
-    }
-    }
+    if (lane == 0) bulk_wait_all();  // stores complete before the CTA exits
   }
   tc_fence_before();
   __syncthreads();
@@ -577,7 +624,7 @@ int make_map(CUtensorMap* tm, const float* base, int64_t inner, int64_t outer, i
   return KB_OK;
 }
 
-// 3-D fp32 tensor map for the C tile store: {N, M, Z} with box {32, 128, 1},
+// 3-D fp32 tensor map for the C tile store: {N, M, Z} with box {32, 32, 1},
 // 128B swizzle (matches the staging layout of the epilogue).
 int make_store_map(CUtensorMap* tm, float* base, int64_t N, int64_t M, int64_t Z, int64_t row_stride,
                    int64_t z_stride) {
@@ -585,7 +632,7 @@ int make_store_map(CUtensorMap* tm, float* base, int64_t N, int64_t M, int64_t Z
   KB_REQUIRE(enc != nullptr, KB_ERR_CUDA, "cuTensorMapEncodeTiled unavailable");
   cuuint64_t dims[3] = {(cuuint64_t)N, (cuuint64_t)M, (cuuint64_t)Z};
   cuuint64_t strides[2] = {(cuuint64_t)row_stride * 4, (cuuint64_t)z_stride * 4};
-  cuuint32_t box[3] = {32, (cuuint32_t)BM, 1};
+  cuuint32_t box[3] = {(cuuint32_t)kBoxCols, (cuuint32_t)kBoxRows, 1};
   cuuint32_t estr[3] = {1, 1, 1};
   CUresult r = enc(tm, CU_TENSOR_MAP_DATA_TYPE_FLOAT32, 3, base, dims, strides, box, estr,
                    CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B,
@@ -679,11 +726,18 @@ int run_gemm(const GemmArgs& g, int splits, float* ws, cudaStream_t s) {
     if (make_store_map(&tc, g.C, g.N, g.M, g.batch, g.ldc, g.batch > 1 ? g.sC : g.ldc * g.M) == KB_OK)
       p.tma_store = 1;
   }
+  p.tiles_n = (int)grid.x;
+  p.tiles_m = (int)grid.y;
+  p.tiles_z = (int)grid.z;
+  // persistent: one CTA per SM (the shared memory and TMEM footprints allow no more)
+  const int64_t ntiles = (int64_t)grid.x * grid.y * grid.z;
+  KB_REQUIRE(ntiles <= 0x7fffffff, KB_ERR_UNSUPPORTED, "gemm: too many tiles");
+  const dim3 pgrid((unsigned)std::min<int64_t>(ntiles, sm_count()), 1, 1);
   int st;
   if (bn256)
-    st = g.trans_a ? launch_tc<256, true>(ta, tb, tc, p, grid, s) : launch_tc<256, false>(ta, tb, tc, p, grid, s);
+    st = g.trans_a ? launch_tc<256, true>(ta, tb, tc, p, pgrid, s) : launch_tc<256, false>(ta, tb, tc, p, pgrid, s);
   else
-    st = g.trans_a ? launch_tc<128, true>(ta, tb, tc, p, grid, s) : launch_tc<128, false>(ta, tb, tc, p, grid, s);
+    st = g.trans_a ? launch_tc<128, true>(ta, tb, tc, p, pgrid, s) : launch_tc<128, false>(ta, tb, tc, p, pgrid, s);
   if (st) return st;
   if (splits > 1) {
     const int64_t total = g.M * g.N;

@@ -321,8 +321,12 @@ def _gemm_check(got, A, B, what, trans=False, batched=False, tol=1e-5):
     assert err < tol, f"{what}: relative error {err:.3e}"
 
 
+# the last four put several tiles on each persistent CTA: 512 tiles of one
+# chunk, 256 tiles of three chunks (the TMEM buffer parity crosses tiles),
+# 256 BN=128 tiles, and a ragged multi-tile case
 @pytest.mark.parametrize("mnk", [(128, 256, 32), (256, 256, 64), (300, 520, 100), (128, 128, 96),
-                                 (1024, 1024, 1024), (2048, 1536, 2048), (129, 257, 33), (64, 40, 8)])
+                                 (1024, 1024, 1024), (2048, 1536, 2048), (129, 257, 33), (64, 40, 8),
+                                 (4096, 4096, 64), (2048, 4096, 320), (32768, 128, 64), (4000, 3000, 200)])
 def test_sgemm_shapes(mnk, cuda_device):
     from kbb200 import ops as K
     from kbb200._lib import read_fault
@@ -335,7 +339,7 @@ def test_sgemm_shapes(mnk, cuda_device):
     assert read_fault() == 0
 
 
-@pytest.mark.parametrize("mnk", [(512, 384, 256), (130, 260, 68)])
+@pytest.mark.parametrize("mnk", [(512, 384, 256), (130, 260, 68), (4096, 2048, 136)])
 def test_sgemm_transposed_a(mnk, cuda_device):
     from kbb200 import ops as K
 
@@ -353,7 +357,7 @@ def test_sgemm_odd_strides_use_cuda_core_path(cuda_device):
     _gemm_check(K.matmul(A, B), A, B, "odd sgemm")
 
 
-@pytest.mark.parametrize("shape", [(4, 256, 384, 512), (3, 128, 96, 256), (2, 130, 70, 40)])
+@pytest.mark.parametrize("shape", [(4, 256, 384, 512), (3, 128, 96, 256), (2, 130, 70, 40), (64, 256, 384, 200)])
 def test_bmm_shapes(shape, cuda_device):
     from kbb200 import ops as K
 
