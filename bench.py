@@ -8,8 +8,11 @@ fraction of the measured roofline, beside the reference arm on the host CPU.
 A step is one pass of the workload family's ops over their benchmark-shape
 inputs (default family "rownorm": LayerNorm and RMSNorm on x[65536, 8192],
 softmax and log-softmax on logits[8192, 32768]).  Inputs are seeded synthetic
-tensors generated on the device, resident before timing, and larger than L2,
-so no flush is needed between steps.  Multi-GPU is weak scaling: every rank
+tensors generated on the device and resident before timing.  Between two
+launches of one op the step moves at least twice the L2 (126 MB) through
+other buffers (the op's own inputs, or the family's other ops); an op for which
+that does not hold gets a 256 MB L2 flush before each launch, outside its
+per-op events but inside the step time.  Multi-GPU is weak scaling: every rank
 runs the full workload on its own GPU (rows are independent; no collective on
 this family), and the step time is the max over ranks.
 
@@ -40,6 +43,8 @@ import torch  # noqa: E402
 PEAKS_FILE = REPO / "MEASURED_PEAKS.json"
 FALLBACK_HBM_GBS = 6650.0
 FALLBACK_BF16_TFLOPS = 1590.0
+L2_BYTES = 126 * 1024 * 1024
+FLUSH_BYTES = 256 * 1024 * 1024
 
 # kernels launched per op call (for gpu_launches)
 LAUNCHES = {"gelu_tanh": 1, "gelu_erf": 1, "swish": 1, "relu": 1, "layer_norm": 1, "rms_norm": 1,
@@ -55,7 +60,10 @@ LAUNCHES = {"gelu_tanh": 1, "gelu_erf": 1, "swish": 1, "relu": 1, "layer_norm": 
 NCU_DRAM_BYTES: dict[str, float | None] = {
     "layer_norm": 4.0 * (536.950528e6 + 483.113216e6),
     "softmax": 4.0 * (268.455168e6 + 209.569536e6),
-    "gelu_tanh": 268.449024e6 + 221.055488e6,
+    "gelu_tanh": 268.47744e6 + 214.69824e6,
+    "diag_matmul": 67.13344e6 + 19.756544e6,
+    # captured on A[8192, 64] (a quarter of the rows), scaled by 4
+    "matmul_small_k": 4.0 * (33.54624e6 + 1015.143e6),
     "sum_dim": 4.0 * (2147.519e6 + 3.969536e6),
     "max_pool2d": 4.0 * (540.104192e6 + 107.429888e6),
     "gemv": 4.0 * (4299.227e6 + 3.568896e6),
@@ -314,8 +322,13 @@ def profile_op(op: str, frac: float, reps: int = 3) -> int:
     dev = torch.device("cuda:0")
     shapes = {}
     for nm, shape, _ in w.inputs:
-        if op == "matmul":
+        if op in ("matmul", "matmul_transposed_a", "matmul_symmetric"):
             shapes[nm] = (4096, 4096)
+        elif op == "matmul_small_k":  # fewer rows of A; K and B unchanged
+            if nm == "A":
+                shapes[nm] = (max(1, int(shape[0] * frac)), shape[1])
+        elif op == "diag_matmul":  # fewer rows of diag(A) and B
+            shapes[nm] = (max(1, int(shape[0] * frac)),) + tuple(shape[1:])
         elif op == "matmul_splitk":
             shapes[nm] = (shape[0], int(shape[1] * frac)) if nm == "A" else (int(shape[0] * frac), shape[1])
         elif nm in ("x", "predictions", "targets", "A", "B") and len(shape) > 1 or nm in ("predictions", "targets"):
@@ -386,7 +399,7 @@ def _main(sink) -> int:
     metric = f"GB/s of algorithmic bytes ({a.workload} family: {', '.join(ops)}); % of B200 roofline"
     config = {"workload": f"{a.workload}: " + "; ".join(
         f"{n} " + "x".join(map(str, WORKLOADS[n].inputs[0][1])) for n in ops),
-        "parallelism": f"weak{world}", "l2": "inputs larger than L2 (126 MB), no flush"}
+        "parallelism": f"weak{world}"}
 
     if a.impl == "reference":
         if rank != 0:
@@ -429,6 +442,15 @@ def _main(sink) -> int:
         if world > 1:
             torch.distributed.barrier(device_ids=[local_rank])
 
+    # L2 hygiene: the bytes that pass between two launches of one op are its
+    # own algorithmic bytes plus those of the family's other ops
+    step_total = sum(w.algo_bytes for _, w, *_ in runners)
+    need_flush = {n for n, w, *_ in runners if step_total < 2 * L2_BYTES}
+    flush_buf = torch.empty(FLUSH_BYTES // 4, dtype=torch.float32, device=device) if need_flush else None
+    config["l2"] = (f"L2 flush ({FLUSH_BYTES >> 20} MB write) before " + ", ".join(sorted(need_flush))
+                    if need_flush else
+                    f"no flush: >= {2 * L2_BYTES >> 20} MB moves between two launches of each op")
+
     stream = torch.cuda.current_stream(device)
     for _ in range(a.warmup):
         for _, _, _, fn, _ in runners:
@@ -445,6 +467,8 @@ def _main(sink) -> int:
     t_start.record(stream)
     for _ in range(a.steps):
         for n, _, _, fn, _ in runners:
+            if n in need_flush:
+                flush_buf.fill_(1.0)
             e0 = torch.cuda.Event(enable_timing=True)
             e1 = torch.cuda.Event(enable_timing=True)
             e0.record(stream)
