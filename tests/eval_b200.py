@@ -11,7 +11,8 @@ every trial and a median / stall flag (:94-123), milestones 1/2/3 (:242-253)
     bit-exact argmax / max-pool) next to the reference's allclose(1e-2);
   - GB/s or TFLOP/s of the candidate and its fraction of the measured B200
     roofline (MEASURED_PEAKS.json);
-  - the torch-eager fp32 CPU time on a bounded sample, with the core count;
+  - the torch-eager fp32 CPU time on a bounded sample (grown until one call
+    takes a quarter second), with the core count;
   - the L2 thrash sized from the device's L2 (2x), not a fixed 256 MB.
 Verdicts keep the reference's JSON fields and add the new ones.  Inputs at
 the benchmark shapes are generated on the device with a seeded generator
@@ -114,41 +115,64 @@ def _close(got, want, tol) -> bool:
     return bool(torch.isclose(got.float(), want.float(), atol=tol, rtol=tol).all())
 
 
-def _cpu_time(name: str, rows: int = 4) -> dict | None:
-    """torch-eager fp32 CPU forward on a bounded sample (leading dim <= rows)."""
-    Model, _, get_init_inputs, _ = problems.load_problem(name)
+def _cpu_sample(name: str, rows: int):
+    """(shapes, fraction of the full workload) for a sample of `rows` along the
+    leading (independent) dimension; None when the op cannot be cut."""
     spec = problems.input_spec(name)
-    shapes = {}
-    frac = 1.0
+    if name in ("6_Matmul_with_large_K_dimension_",):
+        return None  # the K dimension cannot be cut without changing the op
+    if name in ("3_Batched_matrix_multiplication",):
+        return {"A": (rows, 512, 1024), "B": (rows, 1024, 512)}, rows / 256
+    if name in ("12_Matmul_with_diagonal_matrices_",):
+        return {"A": (rows,), "B": (rows, 4096)}, rows / 4096
+    shapes, frac = {}, 1.0
     for nm, shape, _, _ in spec:
         if len(shape) >= 2 and nm in ("x", "A") and shape[0] > rows:
             frac = rows / shape[0]
             shapes[nm] = (rows,) + tuple(shape[1:])
-        elif nm in ("predictions", "targets") and shape[0] > (1 << 22):
-            frac = (1 << 22) / shape[0]
-            shapes[nm] = (1 << 22,)
-    if name in ("6_Matmul_with_large_K_dimension_",):
-        return None  # the K dimension cannot be cut without changing the op
-    if name in ("3_Batched_matrix_multiplication",):
-        shapes = {"A": (rows, 512, 1024), "B": (rows, 1024, 512)}
-        frac = rows / 256
-    if name in ("12_Matmul_with_diagonal_matrices_",):
-        shapes = {"A": (rows * 64,), "B": (rows * 64, 4096)}
-        frac = rows * 64 / 4096
-    Model, get_inputs, get_init_inputs, _ = problems.load_problem(name, shapes)
-    torch.manual_seed(0)
-    ins = get_inputs()
-    m = Model(*get_init_inputs())
+        elif nm in ("predictions", "targets") and shape[0] > rows * 4096:
+            frac = rows * 4096 / shape[0]
+            shapes[nm] = (rows * 4096,)
+    return shapes, frac
+
+
+def _cpu_time(name: str, target_s: float = 0.2, max_bytes: int = 512 << 20) -> dict | None:
+    """torch-eager fp32 CPU forward on a bounded sample of the leading
+    dimension, grown 4x at a time until one call takes >= target_s (so fixed
+    per-call overhead does not inflate the full-size estimate), the sample is
+    the whole tensor, or the next sample's inputs would pass max_bytes."""
     torch.set_num_threads(os.cpu_count() or 1)
-    with torch.no_grad():
-        m(*ins)
-        t0 = time.perf_counter()
-        reps = 3
-        for _ in range(reps):
+    full_bytes = sum(4 * math.prod(shape) for _, shape, _, _ in problems.input_spec(name))
+    rows, best = 4, None
+    while True:
+        cut = _cpu_sample(name, rows)
+        if cut is None:
+            return None
+        shapes, frac = cut
+        Model, get_inputs, get_init_inputs, _ = problems.load_problem(name, shapes)
+        torch.manual_seed(0)
+        ins = get_inputs()
+        m = Model(*get_init_inputs())
+        with torch.no_grad():
             m(*ins)
-        dt = (time.perf_counter() - t0) / reps
-    return {"sample_ms": round(dt * 1e3, 3), "sample_fraction": frac,
-            "full_ms_estimate": round(dt * 1e3 / frac, 3), "cores": os.cpu_count()}
+            t0 = time.perf_counter()
+            m(*ins)
+            dt = time.perf_counter() - t0
+            done = dt >= target_s or frac >= 1.0 or full_bytes * min(1.0, 4 * frac) > max_bytes
+            reps = 1
+            if done and dt < target_s:  # final sample: repeat it up to target_s of work
+                reps = min(50, max(1, math.ceil(target_s / max(dt, 1e-6))))
+                t0 = time.perf_counter()
+                for _ in range(reps):
+                    m(*ins)
+                dt = (time.perf_counter() - t0) / reps
+        best = {"sample_ms": round(dt * 1e3, 3), "sample_fraction": frac, "sample_rows": rows,
+                "sample_reps": reps, "full_ms_estimate": round(dt * 1e3 / frac, 3),
+                "cores": os.cpu_count()}
+        del ins, m
+        if done:
+            return best
+        rows *= 4
 
 
 def evaluate(name: str, out_path: str | None = None, small: bool = False, trials: int = TRIALS,
