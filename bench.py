@@ -51,7 +51,8 @@ LAUNCHES = {"gelu_tanh": 1, "gelu_erf": 1, "swish": 1, "relu": 1, "layer_norm": 
             "softmax": 1, "log_softmax": 1, "sum_dim": 1, "mean_dim": 1, "argmax_dim": 1,
             "mse_loss": 2, "frobenius_normalize": 2, "max_pool2d": 1, "batch_norm_train": 2,
             "matmul": 1, "bmm": 1, "matmul_splitk": 2, "gemv": 1, "matmul_transposed_a": 1,
-            "matmul_symmetric": 1, "diag_matmul": 1, "matmul_small_k": 1}
+            "matmul_symmetric": 1, "diag_matmul": 1, "matmul_small_k": 1,
+            "avg_pool2d": 1, "cumsum": 1, "cross_entropy": 2}
 
 # DRAM bytes per full-size launch (dram__bytes_read.sum + dram__bytes_write.sum)
 # from the ncu captures summarised in profiles/: captured on a quarter of the
@@ -74,7 +75,8 @@ NCU_DRAM_BYTES: dict[str, float | None] = {
 CPU_SAMPLE_ROWS = {"layer_norm": 1024, "rms_norm": 1024, "softmax": 256, "log_softmax": 256,
                    "gelu_tanh": 512, "gelu_erf": 512, "swish": 512, "relu": 512,
                    "sum_dim": 4, "mean_dim": 4, "argmax_dim": 4, "frobenius_normalize": 8,
-                   "max_pool2d": 1, "batch_norm_train": 2}
+                   "max_pool2d": 1, "batch_norm_train": 2, "avg_pool2d": 1, "cumsum": 256,
+                   "cross_entropy": 1024}
 
 
 def load_peaks() -> dict:
@@ -227,6 +229,17 @@ def make_runner(name: str, inputs: list, world: int, rank: int):
     if name in ("matmul_symmetric", "matmul_small_k"):
         y = torch.empty(x.shape[0], inputs[1].shape[1], device=x.device)
         return (lambda: K.matmul(x, inputs[1], out=y)), y
+    if name == "avg_pool2d":
+        e = w.extra
+        N, C, H, W = x.shape
+        y = torch.empty(N, C, H // 2, W // 2, device=x.device)
+        return (lambda: K.avg_pool2d(x, e["kernel_size"], e["stride"], e["padding"], out=y)), y
+    if name == "cumsum":
+        y = torch.empty_like(x)
+        return (lambda: K.cumsum(x, 1, out=y)), y
+    if name == "cross_entropy":
+        y = torch.empty((), device=x.device)
+        return (lambda: K.cross_entropy(x, inputs[1], out=y)), y
     if name == "diag_matmul":
         y = torch.empty_like(inputs[1])
         return (lambda: K.diag_matmul(x, inputs[1], out=y)), y

@@ -218,6 +218,33 @@ KB_API int kb_gemm_splitk_3xtf32(const float* A, const float* B, float* C,
 KB_API int kb_gemv_f32(const float* A, const float* x, float* y, int64_t M,
                 int64_t K, kbStream stream);
 
+/* ---- problems the reference lists but never attempted ------------------
+ * harness/problems.py:45-56 names 45_Average_Pooling_2D, 89_cumsum and
+ * 95_CrossEntropyLoss, and scripts/milestone_table.py:16-24 marks them not
+ * attempted, so these entries replace no reference entry; they follow the
+ * torch semantics named on each.                                          */
+/* torch.nn.functional.avg_pool2d (floor mode) over NCHW: the window sum
+ * (padding counts as 0) divided by the window's size clipped to the padded
+ * input (count_include_pad != 0), to the real input (count_include_pad == 0),
+ * or by divisor_override when it is nonzero.                              */
+KB_API int kb_avgpool2d_f32(const float* x, float* y, int64_t N, int64_t C,
+                     int64_t H, int64_t W, int64_t OH, int64_t OW, int kernel,
+                     int stride, int pad, int count_include_pad,
+                     int divisor_override, kbStream stream);
+/* torch.cumsum(x, dim) for x viewed as [outer, len, inner] with dim the
+ * middle axis: y[o, i, j] = sum_{k <= i} x[o, k, j] (inclusive).          */
+KB_API int kb_cumsum_f32(const float* x, float* y, int64_t outer, int64_t len,
+                  int64_t inner, kbStream stream);
+/* torch.nn.functional.cross_entropy(logits[rows, classes], targets[rows]
+ * int64, reduction='mean', ignore_index): out[0] = mean over rows whose
+ * target is not ignore_index of logsumexp(logits[i]) - logits[i, t_i];
+ * deterministic.  A target outside [0, classes) gives NaN.                */
+KB_API size_t kb_cross_entropy_workspace_size(int64_t rows);
+KB_API int kb_cross_entropy_f32(const float* logits, const int64_t* targets,
+                         float* out, int64_t rows, int64_t classes,
+                         int64_t ignore_index, void* workspace,
+                         size_t workspace_bytes, kbStream stream);
+
 #ifdef __cplusplus
 }
 #endif

@@ -58,6 +58,11 @@ SIGNATURES: dict[str, tuple] = {
     "kb_gemm_splitk_workspace_size": (_sz, [_i64, _i64, _i64]),
     "kb_gemm_splitk_3xtf32": (_int, [_p, _p, _p, _i64, _i64, _i64, _p, _sz, _p]),
     "kb_gemv_f32": (_int, [_p, _p, _p, _i64, _i64, _p]),
+    "kb_avgpool2d_f32": (_int, [_p, _p, _i64, _i64, _i64, _i64, _i64, _i64, _int, _int, _int, _int, _int,
+                                _p]),
+    "kb_cumsum_f32": (_int, [_p, _p, _i64, _i64, _i64, _p]),
+    "kb_cross_entropy_workspace_size": (_sz, [_i64]),
+    "kb_cross_entropy_f32": (_int, [_p, _p, _p, _i64, _i64, _i64, _p, _sz, _p]),
 }
 
 

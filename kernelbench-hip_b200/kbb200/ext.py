@@ -147,3 +147,23 @@ def smallk_gemm_entry(A, B, C) -> None:
     """candidates/7_Matmul_with_small_K_dimension_/v1.py — C = A @ B with a
     small K; served by the 3xTF32 tcgen05 GEMM."""
     ops.matmul(A, B, out=C)
+
+
+# Entries for the problems the reference lists but never attempted
+# (harness/problems.py:45-56, scripts/milestone_table.py:16-24): no reference
+# entry exists, so these follow the same convention (outputs preallocated,
+# asynchronous, no return value) with names of the same style.
+def avgpool_entry(x, y, K: int, pad: int, stride: int | None = None, count_include_pad: int = 1,
+                  divisor_override: int = 0) -> None:
+    """y = avg_pool2d(x, K, stride, pad) on NCHW (floor mode)."""
+    ops.avg_pool2d(x, K, stride, pad, bool(count_include_pad), divisor_override or None, out=y)
+
+
+def cumsum_entry(x, y, dim: int) -> None:
+    """y = torch.cumsum(x, dim)."""
+    ops.cumsum(x, dim, out=y)
+
+
+def cross_entropy_entry(logits, targets, out, ignore_index: int = -100) -> None:
+    """out (0-d) = cross_entropy(logits, targets), mean over non-ignored rows."""
+    ops.cross_entropy(logits, targets, ignore_index, out=out)

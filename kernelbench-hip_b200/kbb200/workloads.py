@@ -27,7 +27,7 @@ F32 = 4
 class Workload:
     name: str                  # op name (kbb200.ops function family)
     problem: str               # candidate / problem id
-    family: str                # gelu | rownorm | reductions | spatial | gemm
+    family: str                # gelu | rownorm | reductions | spatial | gemm | structured | adjacent
     inputs: tuple              # ((name, shape, dist), ...)
     algo_bytes: int            # bytes per launch (see module doc)
     flops: int = 0             # useful FLOPs per launch (contractions)
@@ -51,6 +51,7 @@ _MSE_N = 1 << 28
 _FRO = (256, 1024, 1024)
 _POOL = (32, 64, 512, 512)
 _BN = (64, 128, 256, 256)
+_CE_ROWS, _CE_CLASSES = 32768, 4096
 
 WORKLOADS: dict[str, Workload] = {w.name: w for w in [
     _ew("gelu_tanh", "88_MinGPTNewGelu"),
@@ -112,6 +113,15 @@ WORKLOADS: dict[str, Workload] = {w.name: w for w in [
     Workload("matmul_small_k", "7_Matmul_with_small_K_dimension_", "structured",
              (("A", (32768, 64), "gemm"), ("B", (64, 32768), "gemm")),
              F32 * (2 * 32768 * 64 + 32768 * 32768), flops=2 * 32768 * 32768 * 64),
+    # problems the reference lists but never attempted
+    Workload("avg_pool2d", "45_Average_Pooling_2D", "adjacent", (("x", _POOL, "normal"),),
+             F32 * (math.prod(_POOL) + math.prod(_POOL) // 4),
+             extra={"kernel_size": 3, "stride": 2, "padding": 1}),
+    Workload("cumsum", "89_cumsum", "adjacent", (("x", (_SM_ROWS, _SM_COLS), "normal"),),
+             2 * F32 * _SM_ROWS * _SM_COLS),
+    Workload("cross_entropy", "95_CrossEntropyLoss", "adjacent",
+             (("predictions", (_CE_ROWS, _CE_CLASSES), "normal"), ("targets", (_CE_ROWS,), "labels")),
+             F32 * _CE_ROWS * _CE_CLASSES + 8 * _CE_ROWS + F32),
 ]}
 
 FAMILIES = {
@@ -121,6 +131,7 @@ FAMILIES = {
     "spatial": ["max_pool2d", "batch_norm_train"],
     "gemm": ["matmul", "bmm", "matmul_splitk", "gemv"],
     "structured": ["matmul_transposed_a", "matmul_symmetric", "diag_matmul", "matmul_small_k"],
+    "adjacent": ["avg_pool2d", "cumsum", "cross_entropy"],
 }
 
 
@@ -143,6 +154,8 @@ def fill_(t: torch.Tensor, dist: str, gen: torch.Generator, fan_in: int = 1) -> 
     if dist == "gemm_sym":  # symmetric, entries ~ N(0, 1/K)
         t.normal_(0.0, 1.0 / math.sqrt(2.0 * t.shape[-1]), generator=gen)
         return t.add_(t.T.clone())
+    if dist == "labels":  # int64 class indices in [0, fan_in)
+        return t.random_(0, fan_in, generator=gen)
     raise ValueError(dist)
 
 
@@ -154,7 +167,11 @@ def make_inputs(w: Workload, device, seed: int = 0, shapes: dict | None = None) 
     out = []
     for name, shape, dist in w.inputs:
         shape = tuple((shapes or {}).get(name, shape))
-        t = torch.empty(shape, device=device, dtype=torch.float32)
-        fan_in = shape[-2] if (dist == "gemm" and name == "B") else (shape[-1] if dist == "gemm" else 1)
+        dtype = torch.int64 if dist == "labels" else torch.float32
+        t = torch.empty(shape, device=device, dtype=dtype)
+        if dist == "labels":  # number of classes: the last dim of the first input
+            fan_in = out[0].shape[-1]
+        else:
+            fan_in = shape[-2] if (dist == "gemm" and name == "B") else (shape[-1] if dist == "gemm" else 1)
         out.append(fill_(t, dist, gen, fan_in))
     return out

@@ -223,3 +223,56 @@ def diag_matmul(a, b):
 def matmul_transposed_a(a_t, b):
     """candidates/16_Matmul_with_transposed_A/v1.py (TRANS_A): A stored [K, M], C = A^T @ B."""
     return _out(_f64(a_t).T @ _f64(b))
+
+
+# ------------------------------ problems the reference lists but never attempted
+# (harness/problems.py:45-56; scripts/milestone_table.py:16-24): restated from
+# the torch functions they name.
+def avg_pool2d(x, kernel_size, stride=None, padding=0, count_include_pad=True, divisor_override=None):
+    """torch.nn.functional.avg_pool2d (floor mode) on NCHW: window sum over
+    the real input (padding counts as 0) divided by the window size clipped to
+    the padded input (count_include_pad), to the real input (otherwise), or
+    by divisor_override."""
+    x = _f64(x)
+    k, s, p = kernel_size, (stride or kernel_size), padding
+    N, C, H, W = x.shape
+    OH = (H + 2 * p - k) // s + 1
+    OW = (W + 2 * p - k) // s + 1
+    xp = np.zeros((N, C, H + 2 * p, W + 2 * p))
+    xp[:, :, p:p + H, p:p + W] = x
+    tot = np.zeros((N, C, OH, OW))
+    for u in range(k):
+        for v in range(k):
+            tot += xp[:, :, u: u + s * (OH - 1) + 1: s, v: v + s * (OW - 1) + 1: s]
+    hs = np.arange(OH) * s - p
+    ws = np.arange(OW) * s - p
+    he, we = np.minimum(hs + k, H + p), np.minimum(ws + k, W + p)
+    if divisor_override:
+        div = np.full((OH, OW), float(divisor_override))
+    elif count_include_pad:
+        div = np.outer(he - hs, we - ws).astype(np.float64)
+    else:
+        div = np.outer(np.minimum(he, H) - np.maximum(hs, 0), np.minimum(we, W) - np.maximum(ws, 0)).astype(np.float64)
+    return _out(tot / div)
+
+
+def cumsum(x, dim):
+    """torch.cumsum(x, dim): inclusive prefix sum, float64 accumulation."""
+    return _out(np.cumsum(_f64(x), axis=dim))
+
+
+def cross_entropy(logits, targets, ignore_index=-100):
+    """torch.nn.functional.cross_entropy(logits[N, C], targets[N]),
+    reduction 'mean': mean over rows with target != ignore_index of
+    logsumexp(logits[i]) - logits[i, t_i]; a target outside [0, C) gives NaN;
+    no valid row gives NaN."""
+    x = _f64(logits)
+    t = np.asarray(targets, dtype=np.int64)
+    m = x.max(axis=1, keepdims=True)
+    lse = (m + np.log(np.exp(x - m).sum(axis=1, keepdims=True)))[:, 0]
+    keep = t != ignore_index
+    ok = keep & (t >= 0) & (t < x.shape[1])
+    picked = np.where(ok, x[np.arange(x.shape[0]), np.clip(t, 0, x.shape[1] - 1)], np.nan)
+    loss = lse - picked
+    with np.errstate(invalid="ignore", divide="ignore"):
+        return _out(loss[keep].sum() / keep.sum())

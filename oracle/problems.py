@@ -164,6 +164,29 @@ class Bmm(nn.Module):
         return torch.bmm(A, B)
 
 
+class AvgPool(nn.Module):
+    def __init__(self, kernel_size: int = 3, stride: int = 2, padding: int = 1):
+        super().__init__()
+        self.pool = nn.AvgPool2d(kernel_size, stride, padding)
+
+    def forward(self, x):
+        return self.pool(x)
+
+
+class Cumsum(nn.Module):
+    def __init__(self, dim: int = 1):
+        super().__init__()
+        self.dim = dim
+
+    def forward(self, x):
+        return torch.cumsum(x, dim=self.dim)
+
+
+class CrossEntropy(nn.Module):
+    def forward(self, predictions, targets):
+        return F.cross_entropy(predictions, targets)
+
+
 # ------------------------------------------------------------------ registry
 # name -> (model class, init inputs, ((input name, shape, dist), ...), small shapes)
 _N_EW = (4096, 16384)
@@ -227,6 +250,20 @@ PROBLEMS.update({
                                          {"A": (300, 64), "B": (64, 520)}),
 })
 
+# problems the reference lists but never attempted (harness/problems.py:45-56,
+# scripts/milestone_table.py:16-24).  Shapes: cross-entropy as the
+# reference's recorded baseline (results/baselines.json: logits [32768,
+# 4096]); average pooling on the max-pooling input with the same window;
+# cumsum along the rows of a 1 GiB matrix, the softmax shape.
+PROBLEMS.update({
+    "45_Average_Pooling_2D": (AvgPool, [3, 2, 1], (("x", (32, 64, 512, 512), "normal"),),
+                              {"x": (2, 3, 128, 128)}),
+    "89_cumsum": (Cumsum, [1], (("x", (8192, 32768), "normal"),), {"x": (5, 9000)}),
+    "95_CrossEntropyLoss": (CrossEntropy, [], (("predictions", (32768, 4096), "normal"),
+                                               ("targets", (32768,), "labels")),
+                            {"predictions": (300, 1000), "targets": (300,)}),
+})
+
 SUBSET = list(PROBLEMS)
 
 
@@ -249,6 +286,8 @@ def draw(shape, dist: str, fan_in: int = 1) -> torch.Tensor:
     if dist == "gemm_sym":  # symmetric, entries ~ N(0, 1/K)
         r = torch.randn(shape) / math.sqrt(shape[-1])
         return (r + r.T) * (0.5 ** 0.5)
+    if dist == "labels":  # class indices in [0, fan_in)
+        return torch.randint(0, fan_in, shape, dtype=torch.int64)
     raise ValueError(dist)
 
 
@@ -262,6 +301,8 @@ def input_spec(name: str, shapes: dict | str | None = None):
         shape = tuple(shapes.get(nm, shape))
         if dist in ("gemm", "gemm_sym"):
             fan_in = shape[-2] if nm == "B" else shape[-1]
+        elif dist == "labels":  # number of classes: the last dim of the first input
+            fan_in = out[0][1][-1]
         else:
             fan_in = 1
         out.append((nm, shape, dist, fan_in))

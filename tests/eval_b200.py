@@ -52,6 +52,11 @@ SEEDS = [0, 1, 2, 3, 4]
 REF_TOL = 1e-2
 WARMUP, TRIALS, DISCARD_FIRST, STALL_RATIO = 5, 100, 1, 3.0
 TIMEOUT_S = 900
+# problems whose op tolerance is checked against the reference model run in
+# float64 on the device: torch's fp32 CUDA cumsum is itself off by ~2e-3 at
+# the benchmark shape, above the 1e-4 the library promises (the reference's
+# own allclose(1e-2) is still checked against the fp32 eager model)
+OP_REFERENCE_F64 = {"89_cumsum"}
 
 
 def _peaks() -> dict:
@@ -125,6 +130,10 @@ def _cpu_sample(name: str, rows: int):
         return {"A": (rows, 512, 1024), "B": (rows, 1024, 512)}, rows / 256
     if name in ("12_Matmul_with_diagonal_matrices_",):
         return {"A": (rows,), "B": (rows, 4096)}, rows / 4096
+    if name in ("95_CrossEntropyLoss",):
+        full = dict((nm, shape) for nm, shape, _, _ in spec)["predictions"]
+        rows = min(rows, full[0])
+        return {"predictions": (rows, full[1]), "targets": (rows,)}, rows / full[0]
     shapes, frac = {}, 1.0
     for nm, shape, _, _ in spec:
         if len(shape) >= 2 and nm in ("x", "A") and shape[0] > rows:
@@ -186,7 +195,8 @@ def evaluate(name: str, out_path: str | None = None, small: bool = False, trials
     _, tol = ORACLE[name]
     l2 = int(torch.cuda.get_device_properties(device).L2_cache_size) * 2
     v = {"problem": name, "candidate": str(path.relative_to(REPO)), "eval_sha": EVAL_SHA,
-         "tol": REF_TOL, "op_tol": tol, "warmup": WARMUP, "trials": trials, "torch": torch.__version__,
+         "tol": REF_TOL, "op_tol": tol,
+         "op_reference": "float64" if name in OP_REFERENCE_F64 else "float32 eager", "warmup": WARMUP, "trials": trials, "torch": torch.__version__,
          "device": torch.cuda.get_device_name(device), "shapes": "small" if small else "benchmark"}
     entry = candidate_entry(src)
     v["static_check"] = static_check(src, entry)
@@ -212,6 +222,8 @@ def evaluate(name: str, out_path: str | None = None, small: bool = False, trials
             torch.cuda.synchronize(device)
             got = cand_model(*inputs)
             torch.cuda.synchronize(device)
+            want_op = (ref_model(*[t.double() if t.is_floating_point() else t for t in inputs]).float()
+                       if name in OP_REFERENCE_F64 else want)
         row = {"seed": seed}
         if [hash_tensor(t) for t in inputs] != pre:
             row.update({"pass": False, "why": "R1 input mutated"})
@@ -219,14 +231,15 @@ def evaluate(name: str, out_path: str | None = None, small: bool = False, trials
             row.update({"pass": False, "why": f"shape {tuple(got.shape)} vs {tuple(want.shape)}"})
         else:
             ref_ok = bool(torch.allclose(got.float(), want.float(), atol=REF_TOL, rtol=REF_TOL))
-            op_ok = _close(got, want, tol)
+            op_ok = _close(got, want_op, tol)
             row.update({"pass": ref_ok and op_ok, "ref_allclose": ref_ok, "op_tolerance": op_ok,
-                        "max_diff": float((got.double() - want.double()).abs().max().item())})
+                        "max_diff": float((got.double() - want.double()).abs().max().item()),
+                        "max_diff_op": float((got.double() - want_op.double()).abs().max().item())})
             if row["pass"]:
                 digests[seed] = digest(got.float())
                 passed += 1
         trials_out.append(row)
-        del inputs, want, got
+        del inputs, want, want_op, got
         torch.cuda.empty_cache()
     inputs0 = _inputs(name, 0, device, small)
     with torch.no_grad():

@@ -7,7 +7,7 @@ These fixtures freeze that reference arm's answers (torch-eager CPU, the
 models in oracle/problems.py) so the oracle and the CUDA kernels are checked
 against the same recorded vectors on any machine.
 
-    python tests/golden/make_golden.py      # rewrites tests/golden/*.npz
+    python tests/golden/make_golden.py [problem ...]   # rewrites tests/golden/*.npz
 """
 from __future__ import annotations
 
@@ -48,6 +48,9 @@ GOLDEN_SHAPES = {
     "13_Matmul_for_symmetric_matrices": {"A": (64, 64), "B": (64, 64)},
     "12_Matmul_with_diagonal_matrices_": {"A": (33,), "B": (33, 257)},
     "7_Matmul_with_small_K_dimension_": {"A": (96, 64), "B": (64, 80)},
+    "45_Average_Pooling_2D": {"x": (2, 3, 34, 64)},
+    "89_cumsum": {"x": (3, 5000)},
+    "95_CrossEntropyLoss": {"predictions": (37, 1000), "targets": (37,)},
 }
 SEED = 0
 
@@ -74,11 +77,12 @@ def fixture_path(name: str) -> Path:
 def main() -> int:
     torch.set_num_threads(1)
     total = 0
-    for name in problems.SUBSET:
+    names = sys.argv[1:] or problems.SUBSET
+    for name in names:
         rec = generate(name)
         np.savez_compressed(fixture_path(name), **rec, torch_version=np.array(torch.__version__))
         total += fixture_path(name).stat().st_size
-    print(f"wrote {len(problems.SUBSET)} fixtures, {total / 1e6:.2f} MB")
+    print(f"wrote {len(names)} fixtures, {total / 1e6:.2f} MB")
     return 0
 
 

@@ -3,7 +3,10 @@
 Tolerances are the ones the operator library promises against the
 torch-eager fp32 reference: atol = rtol = 1e-5 for elementwise and
 normalisation outputs, 1e-3 for reductions and contractions, bit-exact for
-argmax indices and max-pooling (whose outputs are input values).
+argmax indices and max-pooling (whose outputs are input values).  Of the
+problems the reference never attempted, average pooling and cross-entropy
+hold 1e-5 and cumsum 1e-4 (a prefix of 32768 N(0,1) terms reaches |y| ~ 500,
+where one fp32 ulp is 3e-5).
 """
 from __future__ import annotations
 
@@ -38,6 +41,9 @@ ORACLE = {
     "13_Matmul_for_symmetric_matrices": (lambda a, b: O.matmul(a, b), 1e-3),
     "12_Matmul_with_diagonal_matrices_": (lambda a, b: O.diag_matmul(a, b), 1e-5),
     "7_Matmul_with_small_K_dimension_": (lambda a, b: O.matmul(a, b), 1e-3),
+    "45_Average_Pooling_2D": (lambda x: O.avg_pool2d(x, 3, 2, 1), 1e-5),
+    "89_cumsum": (lambda x: O.cumsum(x, 1), 1e-4),
+    "95_CrossEntropyLoss": (lambda p, t: O.cross_entropy(p, t), 1e-5),
 }
 
 
@@ -69,6 +75,9 @@ def gpu_call(name: str):
         "13_Matmul_for_symmetric_matrices": lambda a, b: K.matmul(a, b),
         "12_Matmul_with_diagonal_matrices_": lambda a, b: K.diag_matmul(a, b),
         "7_Matmul_with_small_K_dimension_": lambda a, b: K.matmul(a, b),
+        "45_Average_Pooling_2D": lambda x: K.avg_pool2d(x, 3, 2, 1),
+        "89_cumsum": lambda x: K.cumsum(x, 1),
+        "95_CrossEntropyLoss": lambda p, t: K.cross_entropy(p, t),
     }
     return table[name]
 

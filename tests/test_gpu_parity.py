@@ -266,6 +266,10 @@ def test_gemv_shapes(mk, cuda_device):
 
 # ------------------------------------------------------------ benchmark shapes vs torch eager
 FULL = [n for n in problems.SUBSET if n not in GEMMS]
+# compared with the reference model run in float64 on the device: torch's CUDA
+# cumsum accumulates in fp32, whose error near zero crossings of a 32768-long
+# prefix exceeds the 1e-4 tolerance (the CPU reference accumulates in double)
+F64_REFERENCE = {"89_cumsum"}
 
 
 @pytest.mark.parametrize("name", FULL)
@@ -279,7 +283,10 @@ def test_full_size_vs_torch_eager(name, cuda_device):
     inputs = make_inputs(w, cuda_device, seed=0)      # seeded on the device
     ref_model = Model(*get_init_inputs()).to(cuda_device)
     with torch.no_grad():
-        want = ref_model(*inputs)
+        if name in F64_REFERENCE:  # torch's fp32 scan is less accurate than the tolerance
+            want = ref_model(*[t.double() for t in inputs]).float()
+        else:
+            want = ref_model(*inputs)
     got = gpu_call(name)(*inputs)
     torch.cuda.synchronize()
     _, tol = ORACLE[name]
@@ -443,3 +450,112 @@ def test_diag_matmul_shapes(shape, cuda_device):
     a, b = torch.randn(shape[0]), torch.randn(shape)
     got = K.diag_matmul(a.to(cuda_device), b.to(cuda_device)).cpu()
     assert torch.equal(got, torch.diag(a) @ b) or torch.allclose(got, a[:, None] * b, atol=0, rtol=0)
+
+
+
+# ------------------------------------------- problems the reference never attempted
+@pytest.mark.parametrize("case", [
+    ((2, 3, 64, 128), 3, 2, 1, True, None),     # strip kernel (W/4 = 32 threads)
+    ((1, 2, 130, 256), 3, 2, 1, True, None),    # strip kernel, odd H, 2 warps
+    ((2, 3, 64, 128), 3, 2, 1, False, None),    # count_include_pad off: generic
+    ((2, 3, 33, 47), 3, 2, 1, True, None),      # ragged: generic
+    ((1, 2, 20, 24), 2, 2, 0, True, None),
+    ((1, 2, 21, 19), 5, 3, 2, False, None),
+    ((1, 2, 21, 19), 4, 1, 2, True, 7),         # divisor_override
+    ((2, 1, 64, 128), 3, 2, 1, True, 9),        # override equal to the window: strip kernel
+])
+def test_avg_pool2d_paths(case, cuda_device):
+    from kbb200 import ops as K
+
+    shape, k, s, p, cip, div = case
+    x = torch.randn(shape)
+    got = K.avg_pool2d(x.to(cuda_device), k, s, p, cip, div).cpu().numpy()
+    assert_close(got, O.avg_pool2d(x.numpy(), k, s, p, cip, div), 1e-5, f"avg_pool2d {case}")
+    ref = F.avg_pool2d(x, k, s, p, count_include_pad=cip, divisor_override=div).numpy()
+    assert_close(got, ref, 1e-5, f"avg_pool2d {case} vs torch")
+
+
+def test_avg_pool2d_special_values(cuda_device):
+    from kbb200 import ops as K
+
+    x = torch.randn(1, 1, 8, 128)
+    x[0, 0, 2, 5] = float("nan")
+    x[0, 0, 6, 40] = float("inf")
+    got = K.avg_pool2d(x.to(cuda_device), 3, 2, 1).cpu()
+    ref = F.avg_pool2d(x, 3, 2, 1)
+    assert torch.equal(torch.isnan(got), torch.isnan(ref))
+    assert torch.equal(torch.isinf(got), torch.isinf(ref))
+    fin = torch.isfinite(ref)
+    assert torch.allclose(got[fin], ref[fin], atol=1e-5, rtol=1e-5)
+
+
+@pytest.mark.parametrize("shape_dim", [
+    ((3, 4), 1), ((3, 1024), 1), ((5, 4096), 1), ((2, 4100), 1), ((3, 9000), 1), ((2, 32768), 1),
+    ((4, 4097), 1),                               # len % 4 != 0: column kernel on rows
+    ((700, 33), 0), ((3, 50, 7), 1), ((2, 3, 5000), -1), ((6,), 0),
+])
+def test_cumsum_paths(shape_dim, cuda_device):
+    from kbb200 import ops as K
+
+    shape, dim = shape_dim
+    x = torch.randn(shape)
+    got = K.cumsum(x.to(cuda_device), dim).cpu().numpy()
+    assert_close(got, O.cumsum(x.numpy(), dim), 1e-4, f"cumsum {shape} dim {dim}")
+
+
+def test_cumsum_unaligned_view_and_specials(cuda_device):
+    from kbb200 import ops as K
+
+    base = torch.randn(3 * 2049 + 1, device=cuda_device)
+    x = base[1:].view(3, 2049)[:, :2048].contiguous()  # aligned copy
+    v = base[1:2049]                                   # 4-byte offset view: column kernel
+    assert_close(K.cumsum(v, 0).cpu().numpy(), O.cumsum(v.cpu().numpy(), 0), 1e-4, "offset view")
+    x[1, 100] = float("nan")
+    x[2, 7] = float("inf")
+    got = K.cumsum(x, 1).cpu()
+    ref = torch.cumsum(x.cpu().double(), 1).float()
+    assert torch.equal(torch.isnan(got), torch.isnan(ref))
+    assert torch.equal(torch.isinf(got), torch.isinf(ref))
+
+
+@pytest.mark.parametrize("nc", [(5, 10), (64, 1000), (37, 1024), (64, 4096), (9, 5000), (4, 16384),
+                                (3, 20000), (2, 16388)])
+def test_cross_entropy_paths(nc, cuda_device):
+    from kbb200 import ops as K
+
+    N, C = nc
+    x = torch.randn(N, C) * 3
+    t = torch.randint(0, C, (N,))
+    got = K.cross_entropy(x.to(cuda_device), t.to(cuda_device)).cpu().numpy()
+    assert_close(got, O.cross_entropy(x.numpy(), t.numpy()), 1e-5, f"cross_entropy {nc}")
+    assert_close(got, F.cross_entropy(x, t).numpy(), 1e-5, f"cross_entropy {nc} vs torch")
+
+
+def test_cross_entropy_ignore_index_and_invalid_targets(cuda_device):
+    from kbb200 import ops as K
+
+    x = torch.randn(20, 300)
+    t = torch.randint(0, 300, (20,))
+    t[[3, 11]] = -100
+    got = K.cross_entropy(x.to(cuda_device), t.to(cuda_device)).item()
+    assert abs(got - F.cross_entropy(x, t).item()) <= 1e-5 * max(1.0, abs(got))
+    t2 = torch.randint(0, 300, (20,))
+    t2[[5, 9]] = 7
+    got = K.cross_entropy(x.to(cuda_device), t2.to(cuda_device), ignore_index=7).item()
+    assert abs(got - F.cross_entropy(x, t2, ignore_index=7).item()) <= 1e-5 * max(1.0, abs(got))
+    all_ignored = torch.full((20,), -100, dtype=torch.int64)
+    assert math.isnan(K.cross_entropy(x.to(cuda_device), all_ignored.to(cuda_device)).item())
+    bad = t.clone()
+    bad[0] = 300                                  # out of range: NaN (torch raises instead)
+    assert math.isnan(K.cross_entropy(x.to(cuda_device), bad.to(cuda_device)).item())
+    assert math.isnan(K.cross_entropy(torch.empty(0, 5, device=cuda_device),
+                                      torch.empty(0, dtype=torch.int64, device=cuda_device)).item())
+
+
+def test_cross_entropy_is_deterministic(cuda_device):
+    from kbb200 import ops as K
+
+    x = torch.randn(4096, 1000, device=cuda_device)
+    t = torch.randint(0, 1000, (4096,), device=cuda_device)
+    a = K.cross_entropy(x, t)
+    assert all(torch.equal(a, K.cross_entropy(x, t)) for _ in range(3))
