@@ -44,6 +44,8 @@ PEAKS_FILE = REPO / "MEASURED_PEAKS.json"
 FALLBACK_HBM_GBS = 6650.0
 FALLBACK_BF16_TFLOPS = 1590.0
 L2_BYTES = 126 * 1024 * 1024
+# ops whose sharded form has a cross-GPU step (kbb200.dist)
+COLLECTIVE_OPS = {"mse_loss", "frobenius_normalize", "batch_norm_train", "matmul_splitk", "cross_entropy"}
 FLUSH_BYTES = 256 * 1024 * 1024
 
 # kernels launched per op call (for gpu_launches)
@@ -53,6 +55,18 @@ LAUNCHES = {"gelu_tanh": 1, "gelu_erf": 1, "swish": 1, "relu": 1, "layer_norm": 
             "matmul": 1, "bmm": 1, "matmul_splitk": 2, "gemv": 1, "matmul_transposed_a": 1,
             "matmul_symmetric": 1, "diag_matmul": 1, "matmul_small_k": 1,
             "avg_pool2d": 1, "cumsum": 1, "cross_entropy": 2}
+# sharded forms (world > 1): partial kernels + finishing kernel, plus the
+# peer-memory all-reduce kernel when the collective is ours (NCCL's own
+# kernels are not counted); split-K: partial GEMM + fused reduction, or
+# GEMM + split reduce before NCCL
+LAUNCHES_SHARDED = {"mse_loss": 3, "frobenius_normalize": 3, "batch_norm_train": 3, "cross_entropy": 3,
+                    "matmul_splitk": 1}
+
+
+def launches(name: str, world: int, collective: str) -> int:
+    if world > 1 and name in LAUNCHES_SHARDED:
+        return LAUNCHES_SHARDED[name] + (1 if collective == "p2p" or name == "matmul_splitk" else 0)
+    return LAUNCHES[name]
 
 # DRAM bytes per full-size launch (dram__bytes_read.sum + dram__bytes_write.sum)
 # from the ncu captures summarised in profiles/: captured on a quarter of the
@@ -157,9 +171,11 @@ class ClockSampler:
 
 
 # ----------------------------------------------------------------- workload plumbing
-def make_runner(name: str, inputs: list, world: int, rank: int):
+def make_runner(name: str, inputs: list, world: int, rank: int, comm=None):
     """Returns (run() -> None, outputs) launching op `name` into preallocated
-    outputs through the public tensor API (kbb200.ops)."""
+    outputs through the public tensor API (kbb200.ops; kbb200.dist for the
+    ops with a cross-GPU step when world > 1, over `comm` if given, else
+    NCCL)."""
     from kbb200 import ops as K
     from kbb200.workloads import WORKLOADS
 
@@ -172,7 +188,7 @@ def make_runner(name: str, inputs: list, world: int, rank: int):
         if name == "frobenius_normalize" and world > 1:
             from kbb200 import dist
 
-            return (lambda: dist.frobenius_normalize(x, out=y)), y
+            return (lambda: dist.frobenius_normalize(x, out=y, comm=comm)), y
         return (lambda: fn(x, out=y)), y
     if name == "layer_norm":
         y = torch.empty_like(x)
@@ -192,7 +208,7 @@ def make_runner(name: str, inputs: list, world: int, rank: int):
         if world > 1:
             from kbb200 import dist
 
-            return (lambda: dist.mse_loss(x, inputs[1], out=y)), y
+            return (lambda: dist.mse_loss(x, inputs[1], out=y, comm=comm)), y
         return (lambda: K.mse_loss(x, inputs[1], out=y)), y
     if name == "max_pool2d":
         e = w.extra
@@ -205,7 +221,7 @@ def make_runner(name: str, inputs: list, world: int, rank: int):
         if world > 1:
             from kbb200 import dist
 
-            return (lambda: dist.batch_norm_train(x, inputs[1], inputs[2], out=y)), y
+            return (lambda: dist.batch_norm_train(x, inputs[1], inputs[2], out=y, comm=comm)), y
         return (lambda: K.batch_norm_train(x, inputs[1], inputs[2], out=y)), y
     if name == "matmul":
         y = torch.empty(x.shape[0], inputs[1].shape[1], device=x.device)
@@ -218,7 +234,7 @@ def make_runner(name: str, inputs: list, world: int, rank: int):
         if world > 1:
             from kbb200 import dist
 
-            return (lambda: dist.matmul_splitk(x, inputs[1], out=y)), y
+            return (lambda: dist.matmul_splitk(x, inputs[1], out=y, comm=comm)), y
         return (lambda: K.matmul_splitk(x, inputs[1], out=y)), y
     if name == "gemv":
         y = torch.empty(x.shape[0], device=x.device)
@@ -239,6 +255,10 @@ def make_runner(name: str, inputs: list, world: int, rank: int):
         return (lambda: K.cumsum(x, 1, out=y)), y
     if name == "cross_entropy":
         y = torch.empty((), device=x.device)
+        if world > 1:
+            from kbb200 import dist
+
+            return (lambda: dist.cross_entropy(x, inputs[1], out=y, comm=comm)), y
         return (lambda: K.cross_entropy(x, inputs[1], out=y)), y
     if name == "diag_matmul":
         y = torch.empty_like(inputs[1])
@@ -396,6 +416,8 @@ def _main(sink) -> int:
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--cpu-steps", type=int, default=3)
     ap.add_argument("--profile-op", default=None, help="run one op 3x on a reduced input (for ncu)")
+    ap.add_argument("--collective", choices=("p2p", "nccl"), default="p2p",
+                    help="cross-GPU sum of the sharded ops: the library's peer-memory kernel or NCCL")
     ap.add_argument("--frac", type=float, default=0.25, help="input fraction for --profile-op")
     a = ap.parse_args()
     if a.profile_op:
@@ -443,12 +465,21 @@ def _main(sink) -> int:
         tdist.init_process_group("nccl", device_id=device, timeout=datetime.timedelta(seconds=120))
     from kbb200.workloads import make_inputs
 
+    # ops with a cross-GPU step sum their partials over peer memory with the
+    # library's own kernel (kbb200.p2p), or over NCCL with --collective nccl
+    comm = None
+    if world > 1 and COLLECTIVE_OPS & set(ops):
+        config["collective"] = a.collective
+        if a.collective == "p2p":
+            from kbb200.p2p import PeerComm
+
+            comm = PeerComm(slot_bytes=1 << 20, timeout_s=10.0, device=device)
     peaks = load_peaks()
     runners = []
     for n in ops:
         w = WORKLOADS[n]
         ins = make_inputs(w, device, seed=rank)
-        fn, out = make_runner(n, ins, world, rank)
+        fn, out = make_runner(n, ins, world, rank, comm)
         runners.append((n, w, ins, fn, out))
 
     def barrier():
@@ -569,6 +600,9 @@ def _main(sink) -> int:
     if world > 1:
         import torch.distributed as tdist
 
+        if comm is not None:
+            comm.check()
+            comm.close()
         tdist.barrier(device_ids=[local_rank])
         tdist.destroy_process_group()
     if rank != 0:
@@ -579,7 +613,7 @@ def _main(sink) -> int:
         "higher_is_better": True, "scaling": "weak", "vs_baseline": None, "dtype": "f32",
         "data": "synthetic (seeded, generated on device)", "config": config,
         "roofline": roof, "cpu_baseline": cpu, "e2e": e2e, "clocks": clk,
-        "gpu_launches": a.steps * sum(LAUNCHES[n] for n in ops), "per_op": per_op,
+        "gpu_launches": a.steps * sum(launches(n, world, a.collective) for n in ops), "per_op": per_op,
         "impl": "ours",
     }
     sink.emit(json.dumps(line))

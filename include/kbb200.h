@@ -244,6 +244,62 @@ KB_API int kb_cross_entropy_f32(const float* logits, const int64_t* targets,
                          float* out, int64_t rows, int64_t classes,
                          int64_t ignore_index, void* workspace,
                          size_t workspace_bytes, kbStream stream);
+/* sharded form: total[0..1] = (sum of row losses, number of rows not
+ * ignored) over this shard (fp64); after a collective has summed the
+ * shards' totals, out[0] = total[0] / total[1].                           */
+KB_API int kb_cross_entropy_partial_f64(const float* logits, const int64_t* targets,
+                                 double* total, int64_t rows, int64_t classes,
+                                 int64_t ignore_index, void* workspace,
+                                 size_t workspace_bytes, kbStream stream);
+KB_API int kb_cross_entropy_finalize_f32(const double* total, float* out, kbStream stream);
+
+/* ---- cross-GPU reduction over peer memory ------------------------------
+ * The sharded forms of MSE, Frobenius, BatchNorm, split-K GEMM and
+ * cross-entropy exchange one small partial per rank.  The reference runs on
+ * one GPU and has no collective; these entries replace the NCCL all_reduce
+ * between each partial entry and its finish entry with one cooperative
+ * kernel over peer memory (CUDA IPC over NVLink, no multicast):
+ *   buffer   kb_p2p_buffer_alloc(kb_p2p_buffer_bytes(slot), &p) on every rank
+ *            (zeroed); kb_p2p_ipc_handle / kb_p2p_ipc_open share it; `bufs`
+ *            is a DEVICE array of the world base pointers (own at [rank]).
+ *   call     every rank makes the same calls in the same order with the
+ *            same epoch, starting at 1 and increasing by 1 per call;
+ *            dst = sum over ranks of src (rank order: bit-identical on all
+ *            ranks).  src may equal dst.
+ *   failure  a wait longer than timeout_ns records (phase << 8 | peer) in
+ *            the fault word (kb_p2p_read_fault) and leaves dst unwritten;
+ *            the buffer set must then be discarded.                       */
+KB_API size_t kb_p2p_header_bytes(void);
+KB_API size_t kb_p2p_buffer_bytes(size_t slot_bytes);
+KB_API int kb_p2p_buffer_alloc(size_t bytes, void** ptr);
+KB_API int kb_p2p_buffer_free(void* ptr);
+KB_API int kb_p2p_ipc_handle(void* ptr, void* handle /* 64 bytes */);
+KB_API int kb_p2p_ipc_open(const void* handle, void** peer_ptr);
+KB_API int kb_p2p_ipc_close(void* peer_ptr);
+KB_API int kb_p2p_read_fault(int clear, int* value);
+KB_API int kb_p2p_allreduce_f64(void* const* bufs, int rank, int world,
+                         size_t buf_bytes, const double* src, double* dst,
+                         int64_t n, unsigned epoch, uint64_t timeout_ns,
+                         kbStream stream);
+KB_API int kb_p2p_allreduce_f32(void* const* bufs, int rank, int world,
+                         size_t buf_bytes, const float* src, float* dst,
+                         int64_t n, unsigned epoch, uint64_t timeout_ns,
+                         kbStream stream);
+/* split-K fused form: this rank's `splits` partial tiles [splits][n] (from
+ * kb_gemm_splitk_partials_3xtf32) are summed in split order, then across
+ * ranks, in one kernel: dst[n] = the full C on every rank.                */
+KB_API int kb_p2p_splitk_allreduce_f32(void* const* bufs, int rank, int world,
+                                size_t buf_bytes, const float* partials,
+                                int splits, float* dst, int64_t n,
+                                unsigned epoch, uint64_t timeout_ns,
+                                kbStream stream);
+/* the K-split partial tiles of C = A[M,K] B[K,N] without their reduction:
+ * workspace[z][M][N] for z < *splits.                                     */
+KB_API size_t kb_gemm_splitk_partials_workspace_size(int64_t M, int64_t N, int64_t K);
+KB_API int kb_gemm_splitk_partials_3xtf32(const float* A, const float* B, int64_t M,
+                                   int64_t N, int64_t K, void* workspace,
+                                   size_t workspace_bytes, int* splits,
+                                   kbStream stream);
 
 #ifdef __cplusplus
 }

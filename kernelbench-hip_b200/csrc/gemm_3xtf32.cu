@@ -680,9 +680,21 @@ int run_simt(const GemmArgs& g, cudaStream_t s) {
 }
 
 // splits > 1: partial tiles go to `ws` and are reduced into C afterwards.
-int run_gemm(const GemmArgs& g, int splits, float* ws, cudaStream_t s) {
+// reduce_into_c false (single-matrix GEMMs only): the partial tiles
+// [splits][M][N] stay in `ws` (one split: C itself goes to ws) and no
+// reduction runs; *splits_out reports how many there are.
+int run_gemm(const GemmArgs& g, int splits, float* ws, cudaStream_t s, bool reduce_into_c = true,
+             int* splits_out = nullptr) {
+  if (splits_out) *splits_out = 1;
   if (g.M == 0 || g.N == 0 || g.batch == 0) return KB_OK;
-  if (!tma_ok(g)) return run_simt(g, s);
+  if (!tma_ok(g)) {
+    if (reduce_into_c) return run_simt(g, s);
+    GemmArgs w = g;
+    w.C = ws;
+    w.ldc = g.N;
+    w.sC = g.M * g.N;
+    return run_simt(w, s);
+  }
   const bool bn256 = g.N > 128;
   const int BN = bn256 ? 256 : 128;
   CUtensorMap ta, tb;
@@ -698,9 +710,10 @@ int run_gemm(const GemmArgs& g, int splits, float* ws, cudaStream_t s) {
   p.N = (int)g.N;
   p.K = (int)g.K;
   dim3 grid((unsigned)ceil_div(g.N, BN), (unsigned)ceil_div(g.M, BM), 1);
-  if (splits > 1) {
+  if (splits > 1 || !reduce_into_c) {
     const int kbps = (int)ceil_div(nk, splits);
     splits = (int)ceil_div(nk, kbps);  // no empty split
+    if (splits_out) *splits_out = splits;
     p.C = ws;
     p.ldc = g.N;
     p.mode = 1;
@@ -739,7 +752,7 @@ int run_gemm(const GemmArgs& g, int splits, float* ws, cudaStream_t s) {
   else
     st = g.trans_a ? launch_tc<128, true>(ta, tb, tc, p, pgrid, s) : launch_tc<128, false>(ta, tb, tc, p, pgrid, s);
   if (st) return st;
-  if (splits > 1) {
+  if (splits > 1 && reduce_into_c) {
     const int64_t total = g.M * g.N;
     const int blocks = (int)std::min<int64_t>(ceil_div(total, 256), (int64_t)sm_count() * 8);
     splitk_reduce_kernel<<<blocks, 256, 0, s>>>(ws, g.C, (int)g.M, (int)g.N, g.ldc, splits);
@@ -818,6 +831,30 @@ int kb_gemm_splitk_3xtf32(const float* A, const float* B, float* C, int64_t M, i
     if (!kb::gemm::tma_ok(g)) sp = 1;
   }
   return kb::gemm::run_gemm(g, sp, static_cast<float*>(workspace), stream);
+}
+
+/* K-split partial tiles only, for a caller that fuses their reduction with
+ * a cross-GPU one: ws[z][M][N] for z < *splits. */
+size_t kb_gemm_splitk_partials_workspace_size(int64_t M, int64_t N, int64_t K) {
+  const int sp = kb::gemm::splitk_count(M, N, K, kb::gemm::kMaxSms);
+  return (size_t)std::max(sp, 1) * M * N * sizeof(float);
+}
+
+int kb_gemm_splitk_partials_3xtf32(const float* A, const float* B, int64_t M, int64_t N, int64_t K,
+                                   void* workspace, size_t workspace_bytes, int* splits, kbStream stream) {
+  const char* name = "kb_gemm_splitk_partials_3xtf32";
+  KB_REQUIRE(M >= 0 && N >= 0 && K >= 0 && splits, KB_ERR_INVALID_ARG, "%s: bad arguments", name);
+  *splits = 1;
+  if (M == 0 || N == 0) return KB_OK;
+  KB_REQUIRE(A && B, KB_ERR_INVALID_ARG, "%s: null pointer", name);
+  kb::gemm::GemmArgs g{A, B, nullptr, 1, M, N, K, K, N, N, M * K, K * N, M * N, false};
+  int sp = kb::gemm::splitk_count(M, N, K, kb::sm_count());
+  if (!kb::gemm::tma_ok(g)) sp = 1;
+  const size_t need = (size_t)sp * M * N * sizeof(float);
+  KB_REQUIRE(workspace && workspace_bytes >= need, KB_ERR_WORKSPACE,
+             "%s: workspace of %zu bytes needed, %zu given", name, need, workspace_bytes);
+  KB_REQUIRE(kb::aligned16(workspace), KB_ERR_INVALID_ARG, "%s: workspace must be 16-byte aligned", name);
+  return kb::gemm::run_gemm(g, sp, static_cast<float*>(workspace), stream, false, splits);
 }
 
 }  // extern "C"

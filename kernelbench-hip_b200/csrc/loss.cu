@@ -193,10 +193,11 @@ constexpr int kFinishThreads = 1024;
 
 constexpr int kFinishUnroll = 8;
 
-// out = sum(part_sum) / sum(part_count) over n partials, in a fixed order
+// out = sum(part_sum) / sum(part_count) over n partials, in a fixed order;
+// with `total` set, the two sums are written there instead (sharded form)
 __global__ void __launch_bounds__(kFinishThreads)
 ce_finish_kernel(const double* __restrict__ part_sum, const double* __restrict__ part_count, int64_t n,
-                 float* __restrict__ out) {
+                 float* __restrict__ out, double* __restrict__ total = nullptr) {
   __shared__ double red[32];
   // kFinishUnroll independent slots per thread in flight; partial sums are
   // combined in a fixed order, so the result does not depend on timing
@@ -222,7 +223,14 @@ ce_finish_kernel(const double* __restrict__ part_sum, const double* __restrict__
   }
   s = block_sum<kFinishThreads>(s, red);
   c = block_sum<kFinishThreads>(c, red);
-  if (threadIdx.x == 0) *out = (float)(s / c);  // all rows ignored: 0 / 0 = NaN, as torch
+  if (threadIdx.x == 0) {
+    if (total) {
+      total[0] = s;
+      total[1] = c;
+    } else {
+      *out = (float)(s / c);  // all rows ignored: 0 / 0 = NaN, as torch
+    }
+  }
 }
 
 template <int NT, int VPT>
@@ -250,14 +258,38 @@ extern "C" {
 
 size_t kb_cross_entropy_workspace_size(int64_t rows) { return rows > 0 ? kb::ce_ws_bytes(rows) : 0; }
 
+static int cross_entropy_impl(const char* name, const float* logits, const int64_t* targets, float* out,
+                              double* total, int64_t rows, int64_t classes, int64_t ignore_index,
+                              void* workspace, size_t workspace_bytes, kbStream stream);
+
 int kb_cross_entropy_f32(const float* logits, const int64_t* targets, float* out, int64_t rows,
                          int64_t classes, int64_t ignore_index, void* workspace, size_t workspace_bytes,
                          kbStream stream) {
-  const char* name = "kb_cross_entropy_f32";
+  KB_REQUIRE(out, KB_ERR_INVALID_ARG, "kb_cross_entropy_f32: null output");
+  return cross_entropy_impl("kb_cross_entropy_f32", logits, targets, out, nullptr, rows, classes,
+                            ignore_index, workspace, workspace_bytes, stream);
+}
+
+int kb_cross_entropy_partial_f64(const float* logits, const int64_t* targets, double* total, int64_t rows,
+                                 int64_t classes, int64_t ignore_index, void* workspace,
+                                 size_t workspace_bytes, kbStream stream) {
+  KB_REQUIRE(total, KB_ERR_INVALID_ARG, "kb_cross_entropy_partial_f64: null output");
+  return cross_entropy_impl("kb_cross_entropy_partial_f64", logits, targets, nullptr, total, rows, classes,
+                            ignore_index, workspace, workspace_bytes, stream);
+}
+
+int kb_cross_entropy_finalize_f32(const double* total, float* out, kbStream stream) {
+  KB_REQUIRE(total && out, KB_ERR_INVALID_ARG, "kb_cross_entropy_finalize_f32: null pointer");
+  kb::ce_finish_kernel<<<1, kb::kFinishThreads, 0, stream>>>(total, total + 1, 1, out, nullptr);
+  return kb::check_launch("kb_cross_entropy_finalize_f32");
+}
+
+static int cross_entropy_impl(const char* name, const float* logits, const int64_t* targets, float* out,
+                              double* total, int64_t rows, int64_t classes, int64_t ignore_index,
+                              void* workspace, size_t workspace_bytes, kbStream stream) {
   KB_REQUIRE(rows >= 0 && classes >= 0, KB_ERR_INVALID_ARG, "%s: negative size", name);
-  KB_REQUIRE(out, KB_ERR_INVALID_ARG, "%s: null output", name);
-  if (rows == 0) {  // mean over nothing: the finish kernel writes 0 / 0 = NaN
-    kb::ce_finish_kernel<<<1, kb::kFinishThreads, 0, stream>>>(nullptr, nullptr, 0, out);
+  if (rows == 0) {  // mean over nothing: 0 / 0 = NaN (sharded form: sum 0, count 0)
+    kb::ce_finish_kernel<<<1, kb::kFinishThreads, 0, stream>>>(nullptr, nullptr, 0, out, total);
     return kb::check_launch(name);
   }
   KB_REQUIRE(classes >= 1, KB_ERR_INVALID_ARG, "%s: no classes", name);
@@ -283,7 +315,7 @@ int kb_cross_entropy_f32(const float* logits, const int64_t* targets, float* out
     parts = rows;
   }
   if (int st = kb::check_launch(name)) return st;
-  kb::ce_finish_kernel<<<1, kb::kFinishThreads, 0, stream>>>(part_sum, part_count, parts, out);
+  kb::ce_finish_kernel<<<1, kb::kFinishThreads, 0, stream>>>(part_sum, part_count, parts, out, total);
   return kb::check_launch(name);
 }
 

@@ -1,0 +1,278 @@
+// p2p.cu — all-reduce over peer GPU memory for the sharded ops, one kernel
+// per call, fused with the local finishing step (for split-K: the reduction
+// of this rank's own K splits).
+//
+// Each rank owns one symmetric buffer (same size on every rank, cudaMalloc'd
+// here, zeroed once), opened by the peers through CUDA IPC (peer access over
+// NVLink; no multicast objects, no NVLS).  Layout:
+//   [0, 4 KiB)        header: flags[2][kMaxRanks] (epoch at which rank p's
+//                     data slot was complete, written by p into every
+//                     rank's header), grid-barrier count and generation
+//   [4 KiB, +cap)     data slot 0
+//   [.., +cap)        data slot 1
+// A call with epoch e uses slot e & 1 and runs as one cooperative kernel
+// (all CTAs co-resident):
+//   1. write this rank's contribution into its own slot (for split-K: the
+//      fixed-order sum of its K-split partial tiles);
+//   2. grid barrier (bounded wait);
+//   3. CTA 0 publishes: system-scope release store of e into flags[slot][rank]
+//      of every rank;
+//   4. every CTA waits (bounded) until flags[slot][p] == e for every p;
+//   5. dst[i] = sum over p = 0 .. world-1 of slot_p[i], in rank order: every
+//      rank computes bit-identical results.
+// Slot reuse is safe: rank p rewrites slot e & 1 only in call e + 2, after
+// its call e + 1 saw every rank's signal, which each rank sends only after
+// its call e (and so its reads of slot e & 1) completed.
+// Every wait is bounded by %globaltimer; on expiry the kernel records a
+// fault word (kb_p2p_read_fault), leaves without writing dst, and the buffer
+// set must be discarded (its barrier state is no longer consistent).
+#include <string.h>
+
+#include "kb_common.cuh"
+
+namespace kb {
+
+__device__ int g_p2p_fault = 0;  // (phase << 8) | peer of the first expired wait, 0 = none
+
+namespace {
+
+constexpr int kMaxRanks = 64;
+constexpr size_t kHeaderBytes = 4096;
+constexpr int kP2PThreads = 256;
+
+struct Header {
+  unsigned flags[2][kMaxRanks];
+  unsigned bar_count;
+  unsigned bar_gen;
+};
+static_assert(sizeof(Header) <= kHeaderBytes, "header");
+
+struct P2PArgs {
+  char* const* bufs;   // device array [world]: base of every rank's buffer (own at [rank])
+  int rank, world;
+  size_t cap;          // bytes per data slot
+  int64_t n;           // elements
+  const void* src;     // mode 0: n elements; mode 1: `splits` fp32 partials of n, stride n
+  int splits;
+  void* dst;
+  unsigned epoch;
+  uint64_t timeout_ns;
+};
+
+__device__ __forceinline__ uint64_t now_ns() {
+  uint64_t t;
+  asm volatile("mov.u64 %0, %%globaltimer;" : "=l"(t));
+  return t;
+}
+__device__ __forceinline__ void store_release_sys(unsigned* p, unsigned v) {
+  asm volatile("st.release.sys.global.u32 [%0], %1;" ::"l"(p), "r"(v) : "memory");
+}
+__device__ __forceinline__ unsigned load_acquire_sys(const unsigned* p) {
+  unsigned v;
+  asm volatile("ld.acquire.sys.global.u32 %0, [%1];" : "=r"(v) : "l"(p) : "memory");
+  return v;
+}
+__device__ __forceinline__ unsigned load_volatile(const unsigned* p) {
+  return *reinterpret_cast<const volatile unsigned*>(p);
+}
+
+// Spin until `ready()`; false (and the fault word set) after timeout_ns or
+// once another CTA has recorded a fault.
+template <class Ready>
+__device__ bool bounded_wait(Ready ready, uint64_t timeout_ns, int code) {
+  if (ready()) return true;
+  const uint64_t t0 = now_ns();
+  for (unsigned it = 1;; ++it) {
+    if (ready()) return true;
+    if ((it & 63) == 0) {
+      if (*reinterpret_cast<volatile int*>(&g_p2p_fault)) return false;
+      if (now_ns() - t0 > timeout_ns) {
+        atomicCAS(&g_p2p_fault, 0, code);
+        return false;
+      }
+    }
+  }
+}
+
+template <class T>
+__device__ __forceinline__ T load_cv(const T* p) {
+  return __ldcv(p);
+}
+
+template <class T, int MODE>
+__global__ void __launch_bounds__(kP2PThreads) p2p_allreduce_kernel(P2PArgs a) {
+  __shared__ int s_ok;
+  const unsigned slot = a.epoch & 1u;
+  Header* mine_h = reinterpret_cast<Header*>(a.bufs[a.rank]);
+  T* mine = reinterpret_cast<T*>(a.bufs[a.rank] + kHeaderBytes + slot * a.cap);
+  const int64_t stride = (int64_t)gridDim.x * blockDim.x;
+  const int64_t i0 = (int64_t)blockIdx.x * blockDim.x + threadIdx.x;
+
+  // 1. this rank's contribution
+  if (MODE == 0) {
+    const T* src = static_cast<const T*>(a.src);
+    for (int64_t i = i0; i < a.n; i += stride) mine[i] = src[i];
+  } else {
+    const float* part = static_cast<const float*>(a.src);
+    for (int64_t i = i0; i < a.n; i += stride) {
+      float s = 0.f;
+#pragma unroll 8
+      for (int z = 0; z < a.splits; ++z) s += part[(int64_t)z * a.n + i];  // split order; loads run ahead
+      mine[i] = s;
+    }
+  }
+
+  // 2. grid barrier (all CTAs are co-resident: cooperative launch)
+  __syncthreads();
+  if (threadIdx.x == 0) {
+    __threadfence();
+    bool ok = true;
+    const unsigned old = atomicAdd(&mine_h->bar_count, 1u);
+    if (old == gridDim.x - 1) {
+      mine_h->bar_count = 0;
+      __threadfence();
+      atomicExch(&mine_h->bar_gen, a.epoch);
+    } else {
+      ok = bounded_wait([&] { return load_volatile(&mine_h->bar_gen) == a.epoch; }, a.timeout_ns,
+                        (1 << 8) | a.rank);
+    }
+    // 3. publish this rank's slot to every rank
+    if (ok && blockIdx.x == 0) {
+      __threadfence_system();
+      for (int p = 0; p < a.world; ++p) {
+        Header* h = reinterpret_cast<Header*>(a.bufs[p]);
+        store_release_sys(&h->flags[slot][a.rank], a.epoch);
+      }
+    }
+    // 4. wait for every rank's slot
+    for (int p = 0; ok && p < a.world; ++p)
+      ok = bounded_wait([&] { return load_acquire_sys(&mine_h->flags[slot][p]) == a.epoch; },
+                        a.timeout_ns, (2 << 8) | p);
+    s_ok = ok ? 1 : 0;
+  }
+  __syncthreads();
+  if (!s_ok) return;
+  __threadfence_system();
+
+  // 5. rank-ordered sum of every rank's slot
+  T* dst = static_cast<T*>(a.dst);
+  for (int64_t i = i0; i < a.n; i += stride) {
+    T acc = T(0);
+    for (int p = 0; p < a.world; ++p)
+      acc += load_cv(reinterpret_cast<const T*>(a.bufs[p] + kHeaderBytes + slot * a.cap) + i);
+    dst[i] = acc;
+  }
+}
+
+template <class T, int MODE>
+int launch_p2p(const char* name, P2PArgs a, cudaStream_t s) {
+  KB_REQUIRE(a.bufs && a.world >= 1 && a.world <= kMaxRanks && a.rank >= 0 && a.rank < a.world,
+             KB_ERR_INVALID_ARG, "%s: bad communicator (rank %d of %d)", name, a.rank, a.world);
+  KB_REQUIRE(a.n >= 0 && (a.n == 0 || (a.src && a.dst)), KB_ERR_INVALID_ARG, "%s: bad buffers", name);
+  KB_REQUIRE((size_t)a.n * sizeof(T) <= a.cap, KB_ERR_WORKSPACE,
+             "%s: %lld elements exceed the %zu-byte slot", name, (long long)a.n, a.cap);
+  auto kern = p2p_allreduce_kernel<T, MODE>;
+  static int per_sm = 0;
+  if (per_sm == 0) {
+    int b = 0;
+    KB_CUDA(cudaOccupancyMaxActiveBlocksPerMultiprocessor(&b, kern, kP2PThreads, 0));
+    per_sm = b > 0 ? b : 1;
+  }
+  // one element per thread (the split-K form reads `splits` partials for
+  // each), capped at what is co-resident
+  const int64_t want = std::max<int64_t>(1, ceil_div(a.n, (int64_t)kP2PThreads));
+  const int grid = (int)std::min<int64_t>(want, (int64_t)sm_count() * per_sm);
+  void* args[] = {&a};
+  KB_CUDA(cudaLaunchCooperativeKernel((const void*)kern, dim3(grid), dim3(kP2PThreads), args, 0, s));
+  return KB_OK;
+}
+
+size_t slot_cap(size_t buf_bytes) {
+  return buf_bytes > kHeaderBytes ? ((buf_bytes - kHeaderBytes) / 2) & ~(size_t)255 : 0;
+}
+
+}  // namespace
+}  // namespace kb
+
+extern "C" {
+
+size_t kb_p2p_header_bytes(void) { return kb::kHeaderBytes; }
+
+size_t kb_p2p_buffer_bytes(size_t slot_bytes) {
+  return kb::kHeaderBytes + 2 * ((slot_bytes + 255) & ~(size_t)255);
+}
+
+int kb_p2p_buffer_alloc(size_t bytes, void** ptr) {
+  KB_REQUIRE(ptr && bytes > kb::kHeaderBytes, KB_ERR_INVALID_ARG, "kb_p2p_buffer_alloc: bad arguments");
+  void* p = nullptr;
+  KB_CUDA(cudaMalloc(&p, bytes));
+  const cudaError_t e = cudaMemset(p, 0, bytes);
+  if (e != cudaSuccess) {
+    cudaFree(p);
+    return kb::set_error(KB_ERR_CUDA, "kb_p2p_buffer_alloc: %s", cudaGetErrorString(e));
+  }
+  KB_CUDA(cudaDeviceSynchronize());
+  *ptr = p;
+  return KB_OK;
+}
+
+int kb_p2p_buffer_free(void* ptr) {
+  if (ptr) KB_CUDA(cudaFree(ptr));
+  return KB_OK;
+}
+
+int kb_p2p_ipc_handle(void* ptr, void* handle) {
+  KB_REQUIRE(ptr && handle, KB_ERR_INVALID_ARG, "kb_p2p_ipc_handle: null pointer");
+  cudaIpcMemHandle_t h;
+  KB_CUDA(cudaIpcGetMemHandle(&h, ptr));
+  memcpy(handle, &h, sizeof(h));
+  return KB_OK;
+}
+
+int kb_p2p_ipc_open(const void* handle, void** peer_ptr) {
+  KB_REQUIRE(handle && peer_ptr, KB_ERR_INVALID_ARG, "kb_p2p_ipc_open: null pointer");
+  cudaIpcMemHandle_t h;
+  memcpy(&h, handle, sizeof(h));
+  KB_CUDA(cudaIpcOpenMemHandle(peer_ptr, h, cudaIpcMemLazyEnablePeerAccess));
+  return KB_OK;
+}
+
+int kb_p2p_ipc_close(void* peer_ptr) {
+  if (peer_ptr) KB_CUDA(cudaIpcCloseMemHandle(peer_ptr));
+  return KB_OK;
+}
+
+int kb_p2p_read_fault(int clear, int* value) {
+  KB_REQUIRE(value, KB_ERR_INVALID_ARG, "kb_p2p_read_fault: null pointer");
+  KB_CUDA(cudaMemcpyFromSymbol(value, kb::g_p2p_fault, sizeof(int)));
+  if (clear) {
+    const int zero = 0;
+    KB_CUDA(cudaMemcpyToSymbol(kb::g_p2p_fault, &zero, sizeof(int)));
+  }
+  return KB_OK;
+}
+
+int kb_p2p_allreduce_f64(void* const* bufs, int rank, int world, size_t buf_bytes, const double* src,
+                         double* dst, int64_t n, unsigned epoch, uint64_t timeout_ns, kbStream stream) {
+  kb::P2PArgs a{reinterpret_cast<char* const*>(bufs), rank, world, kb::slot_cap(buf_bytes), n, src, 0, dst,
+                epoch, timeout_ns};
+  return kb::launch_p2p<double, 0>("kb_p2p_allreduce_f64", a, stream);
+}
+
+int kb_p2p_allreduce_f32(void* const* bufs, int rank, int world, size_t buf_bytes, const float* src,
+                         float* dst, int64_t n, unsigned epoch, uint64_t timeout_ns, kbStream stream) {
+  kb::P2PArgs a{reinterpret_cast<char* const*>(bufs), rank, world, kb::slot_cap(buf_bytes), n, src, 0, dst,
+                epoch, timeout_ns};
+  return kb::launch_p2p<float, 0>("kb_p2p_allreduce_f32", a, stream);
+}
+
+int kb_p2p_splitk_allreduce_f32(void* const* bufs, int rank, int world, size_t buf_bytes, const float* partials,
+                                int splits, float* dst, int64_t n, unsigned epoch, uint64_t timeout_ns,
+                                kbStream stream) {
+  KB_REQUIRE(splits >= 1, KB_ERR_INVALID_ARG, "kb_p2p_splitk_allreduce_f32: splits < 1");
+  kb::P2PArgs a{reinterpret_cast<char* const*>(bufs), rank, world, kb::slot_cap(buf_bytes), n, partials,
+                splits, dst, epoch, timeout_ns};
+  return kb::launch_p2p<float, 1>("kb_p2p_splitk_allreduce_f32", a, stream);
+}
+
+}  // extern "C"

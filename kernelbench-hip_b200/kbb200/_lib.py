@@ -63,6 +63,22 @@ SIGNATURES: dict[str, tuple] = {
     "kb_cumsum_f32": (_int, [_p, _p, _i64, _i64, _i64, _p]),
     "kb_cross_entropy_workspace_size": (_sz, [_i64]),
     "kb_cross_entropy_f32": (_int, [_p, _p, _p, _i64, _i64, _i64, _p, _sz, _p]),
+    "kb_cross_entropy_partial_f64": (_int, [_p, _p, _p, _i64, _i64, _i64, _p, _sz, _p]),
+    "kb_cross_entropy_finalize_f32": (_int, [_p, _p, _p]),
+    "kb_p2p_header_bytes": (_sz, []),
+    "kb_p2p_buffer_bytes": (_sz, [_sz]),
+    "kb_p2p_buffer_alloc": (_int, [_sz, C.POINTER(C.c_void_p)]),
+    "kb_p2p_buffer_free": (_int, [_p]),
+    "kb_p2p_ipc_handle": (_int, [_p, _p]),
+    "kb_p2p_ipc_open": (_int, [_p, C.POINTER(C.c_void_p)]),
+    "kb_p2p_ipc_close": (_int, [_p]),
+    "kb_p2p_read_fault": (_int, [_int, C.POINTER(C.c_int)]),
+    "kb_p2p_allreduce_f64": (_int, [_p, _int, _int, _sz, _p, _p, _i64, C.c_uint, C.c_uint64, _p]),
+    "kb_p2p_allreduce_f32": (_int, [_p, _int, _int, _sz, _p, _p, _i64, C.c_uint, C.c_uint64, _p]),
+    "kb_p2p_splitk_allreduce_f32": (_int, [_p, _int, _int, _sz, _p, _int, _p, _i64, C.c_uint, C.c_uint64,
+                                           _p]),
+    "kb_gemm_splitk_partials_workspace_size": (_sz, [_i64, _i64, _i64]),
+    "kb_gemm_splitk_partials_3xtf32": (_int, [_p, _p, _i64, _i64, _i64, _p, _sz, C.POINTER(C.c_int), _p]),
 }
 
 

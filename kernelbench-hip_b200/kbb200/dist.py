@@ -10,12 +10,16 @@ partial kernel and a local finishing kernel (the split C-ABI entry pairs):
     mse_loss           sum (a-b)^2  (fp64)      all_reduce 8 B        divide by total count
     frobenius          sum x^2      (fp64)      all_reduce 8 B        x / sqrt(total)
     batch_norm_train   per-channel sum, sum^2   all_reduce 16*C B     normalise + affine
+    cross_entropy      sum of losses, count     all_reduce 16 B       divide
     matmul_splitk      partial C over K slice   all_reduce M*N*4 B    (result replicated)
 
-Collectives go through torch.distributed (NCCL over NVLink on B200s).  The
-per-shard kernels are injectable (`kernels=`) so the composition can be
-tested with CPU implementations on a gloo process group; by default they are
-the CUDA kernels of kbb200.ops.
+The collective is either torch.distributed's all_reduce (NCCL over NVLink on
+B200s; gloo on CPU) or, given `comm=PeerComm(...)` (kbb200.p2p), the
+library's own all-reduce kernel over peer memory; for split-K that kernel
+also performs the rank's own K-split reduction, so local finish and
+cross-GPU sum are one launch.  The per-shard kernels are injectable
+(`kernels=`) so the composition can be tested with CPU implementations on a
+gloo process group; by default they are the CUDA kernels of kbb200.ops.
 """
 from __future__ import annotations
 
@@ -50,7 +54,9 @@ def shard(t: torch.Tensor, rank: int, world: int, dim: int = 0) -> torch.Tensor:
     return t.narrow(dim, lo, hi - lo)
 
 
-def _all_reduce_sum(t: torch.Tensor, group=None) -> torch.Tensor:
+def _all_reduce_sum(t: torch.Tensor, group=None, comm=None) -> torch.Tensor:
+    if comm is not None:
+        return comm.all_reduce_(t)
     if _world(group)[1] > 1:
         tdist.all_reduce(t, op=tdist.ReduceOp.SUM, group=group)
     return t
@@ -66,46 +72,64 @@ def global_count(local: int, device, group=None) -> int:
 
 
 def mse_loss(a: torch.Tensor, b: torch.Tensor, total_n: int | None = None, out=None, group=None,
-             kernels=None):
+             kernels=None, comm=None):
     """mean((a - b)^2) over the union of all ranks' shards (replicated 0-d
     result).  total_n defaults to world_size * a.numel() (equal shards)."""
     k = kernels or _default_kernels()
     _, world = _world(group)
     part = k.mse_partial(a, b)
-    _all_reduce_sum(part, group)
+    _all_reduce_sum(part, group, comm)
     n = total_n if total_n is not None else a.numel() * world
     return k.mse_finalize(part, n, out=out)
 
 
-def frobenius_normalize(x: torch.Tensor, out=None, group=None, kernels=None):
+def frobenius_normalize(x: torch.Tensor, out=None, group=None, kernels=None, comm=None):
     """x_shard / ||x||_F where the norm spans all ranks' shards."""
     k = kernels or _default_kernels()
     part = k.sumsq_partial(x)
-    _all_reduce_sum(part, group)
+    _all_reduce_sum(part, group, comm)
     return k.scale_by_inv_norm(x, part, out=out)
 
 
 def batch_norm_train(x: torch.Tensor, weight=None, bias=None, eps: float = 1e-5,
                      momentum: float = 0.1, running_mean=None, running_var=None, out=None,
-                     total_count: int | None = None, group=None, kernels=None):
+                     total_count: int | None = None, group=None, kernels=None, comm=None):
     """Training-mode BatchNorm with statistics over the global batch (every
     rank holds a slice of the batch dim): SyncBatchNorm semantics, equal to
     BatchNorm on the concatenated batch."""
     k = kernels or _default_kernels()
     _, world = _world(group)
     stats = k.batch_norm_stats(x)
-    _all_reduce_sum(stats, group)
+    _all_reduce_sum(stats, group, comm)
     per_rank = x.shape[0] * math.prod(x.shape[2:])
     count = total_count if total_count is not None else per_rank * world
     return k.batch_norm_apply(x, stats, count, weight, bias, eps, momentum, running_mean,
                               running_var, out=out)
 
 
-def matmul_splitk(a: torch.Tensor, b: torch.Tensor, out=None, group=None, kernels=None):
+def matmul_splitk(a: torch.Tensor, b: torch.Tensor, out=None, group=None, kernels=None, comm=None):
     """C = A @ B with K sharded: rank r holds A[:, K_r] and B[K_r, :].  Each
     rank computes its partial C (split-K across its own SMs as well), then one
-    all_reduce sums the partials; every rank ends with the full C."""
+    all_reduce sums the partials; every rank ends with the full C.  With a
+    PeerComm the rank's K-split tiles go straight into the peer all-reduce
+    kernel, which sums them (split order) and then across ranks (rank order)."""
     k = kernels or _default_kernels()
+    if comm is not None:
+        parts, splits = k.matmul_splitk_partials(a, b)
+        c = out if out is not None else torch.empty(a.shape[0], b.shape[1], device=a.device,
+                                                    dtype=torch.float32)
+        return comm.splitk_all_reduce(parts, splits, c)
     c = k.matmul_splitk(a, b, out=out)
     _all_reduce_sum(c, group)
     return c
+
+
+def cross_entropy(logits: torch.Tensor, targets: torch.Tensor, ignore_index: int = -100, out=None,
+                  group=None, kernels=None, comm=None):
+    """Mean cross-entropy over the union of all ranks' row shards (replicated
+    0-d result): per-shard (sum of losses, rows not ignored), one all_reduce
+    of those 16 bytes, then the division."""
+    k = kernels or _default_kernels()
+    part = k.cross_entropy_partial(logits, targets, ignore_index)
+    _all_reduce_sum(part, group, comm)
+    return k.cross_entropy_finalize(part, out=out)

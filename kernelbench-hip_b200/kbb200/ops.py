@@ -9,6 +9,7 @@ raises KbError; nothing falls back to another implementation.
 """
 from __future__ import annotations
 
+import ctypes as C
 import math
 
 import torch
@@ -449,10 +450,7 @@ def cumsum(x, dim: int, out=None):
     return y
 
 
-def cross_entropy(logits, targets, ignore_index: int = -100, out=None):
-    """torch.nn.functional.cross_entropy(logits[N, C], targets[N] int64),
-    reduction 'mean', no class weights, no label smoothing; a 0-d result."""
-    fn = "kb_cross_entropy_f32"
+def _ce_args(fn, logits, targets):
     _check_f32(fn, logits)
     if logits.dim() != 2:
         raise RuntimeError(f"{fn}: expected logits [N, C], got {tuple(logits.shape)}")
@@ -460,11 +458,53 @@ def cross_entropy(logits, targets, ignore_index: int = -100, out=None):
         raise RuntimeError(f"{fn}: targets must be an int64 tensor")
     if targets.device != logits.device or not targets.is_contiguous():
         raise RuntimeError(f"{fn}: targets must be contiguous and on {logits.device}")
-    N, Cc = logits.shape
-    if targets.numel() != N:
-        raise RuntimeError(f"{fn}: {targets.numel()} targets for {N} rows")
+    if targets.numel() != logits.shape[0]:
+        raise RuntimeError(f"{fn}: {targets.numel()} targets for {logits.shape[0]} rows")
+    return logits.shape
+
+
+def cross_entropy_partial(logits, targets, ignore_index: int = -100, partial=None):
+    """fp64 (sum of row losses, rows not ignored) of this shard, for a
+    cross-GPU sum before cross_entropy_finalize."""
+    fn = "kb_cross_entropy_partial_f64"
+    N, Cc = _ce_args(fn, logits, targets)
+    p = partial if partial is not None else torch.empty(2, device=logits.device, dtype=torch.float64)
+    ws = _workspace(logits, LIB.kb_cross_entropy_workspace_size(N))
+    check(fn, LIB.kb_cross_entropy_partial_f64(logits.data_ptr(), targets.data_ptr(), p.data_ptr(), N, Cc,
+                                               int(ignore_index), ws.data_ptr(), ws.numel(), _stream(logits)))
+    return p
+
+
+def cross_entropy_finalize(total: torch.Tensor, out=None):
+    fn = "kb_cross_entropy_finalize_f32"
+    y = out if out is not None else torch.empty((), device=total.device, dtype=torch.float32)
+    check(fn, LIB.kb_cross_entropy_finalize_f32(total.data_ptr(), y.data_ptr(), _stream(total)))
+    return y
+
+
+def cross_entropy(logits, targets, ignore_index: int = -100, out=None):
+    """torch.nn.functional.cross_entropy(logits[N, C], targets[N] int64),
+    reduction 'mean', no class weights, no label smoothing; a 0-d result."""
+    fn = "kb_cross_entropy_f32"
+    N, Cc = _ce_args(fn, logits, targets)
     y = _out_like(logits, out, fn, ())
     ws = _workspace(logits, LIB.kb_cross_entropy_workspace_size(N))
     check(fn, LIB.kb_cross_entropy_f32(logits.data_ptr(), targets.data_ptr(), y.data_ptr(), N, Cc,
                                        int(ignore_index), ws.data_ptr(), ws.numel(), _stream(logits)))
     return y
+
+
+def matmul_splitk_partials(A, B):
+    """The K-split partial tiles of A @ B without their reduction:
+    (partials [splits, M, N], splits), for a fused cross-GPU reduction."""
+    fn = "kb_gemm_splitk_partials_3xtf32"
+    _check_f32(fn, A, B)
+    M, K = A.shape
+    if B.shape[0] != K:
+        raise RuntimeError(f"{fn}: inner dimensions differ")
+    N = B.shape[1]
+    ws = _workspace(A, LIB.kb_gemm_splitk_partials_workspace_size(M, N, K))
+    sp = C.c_int(1)
+    check(fn, LIB.kb_gemm_splitk_partials_3xtf32(A.data_ptr(), B.data_ptr(), M, N, K, ws.data_ptr(),
+                                                 ws.numel(), C.byref(sp), _stream(A)))
+    return ws, sp.value

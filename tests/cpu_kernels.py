@@ -63,3 +63,20 @@ def matmul_splitk(a, b, out=None):
         out.copy_(r)
         return out
     return r
+
+
+def cross_entropy_partial(logits, targets, ignore_index=-100):
+    x = logits.double()
+    keep = targets != ignore_index
+    lse = torch.logsumexp(x, dim=1)
+    picked = x.gather(1, targets.clamp(0, x.shape[1] - 1).unsqueeze(1)).squeeze(1)
+    loss = torch.where(keep, lse - picked, torch.zeros_like(lse))
+    return torch.stack([loss.sum(), keep.double().sum()])
+
+
+def cross_entropy_finalize(total, out=None):
+    y = (total[0] / total[1]).float()
+    if out is not None:
+        out.copy_(y)
+        return out
+    return y

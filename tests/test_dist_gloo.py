@@ -68,6 +68,12 @@ def _worker(rank, world, port, case, q):
             got = dist.matmul_splitk(dist.shard(A, rank, world, dim=1), dist.shard(B, rank, world, dim=0),
                                      kernels=CK)
             res = (got.numpy(), O.matmul(A.numpy(), B.numpy()))
+        elif case == "crossentropy":
+            x = torch.randn(11, 30, generator=g) * 2
+            t = torch.randint(0, 30, (11,), generator=g)
+            t[[2, 9]] = -100                                   # ignored rows on both shards
+            got = dist.cross_entropy(dist.shard(x, rank, world), dist.shard(t, rank, world), kernels=CK)
+            res = (float(got), float(O.cross_entropy(x.numpy(), t.numpy())))
         elif case == "count":
             res = (dist.global_count(10 + rank, "cpu"), 10 * world + sum(range(world)))
         elif case == "rank_fails":
@@ -102,12 +108,12 @@ def _run(case, world=2, timeout=60):
     return out
 
 
-@pytest.mark.parametrize("case", ["mse", "frobenius", "batchnorm", "splitk", "count"])
+@pytest.mark.parametrize("case", ["mse", "frobenius", "batchnorm", "splitk", "crossentropy", "count"])
 def test_sharded_composition_matches_oracle(case):
     out = _run(case)
     for rank, (status, res) in out.items():
         assert status == "ok", res
-        if case == "mse":
+        if case in ("mse", "crossentropy"):
             np.testing.assert_allclose(res[0], res[1], rtol=1e-6)
         elif case == "batchnorm":
             np.testing.assert_allclose(res[0], res[1], rtol=1e-5, atol=1e-5)

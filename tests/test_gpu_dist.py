@@ -3,7 +3,9 @@ per-shard kernels reproduce the single-device answer on the global input.
 
 Each rank builds the same seeded global tensors on the CPU, keeps its shard
 on its own GPU, runs the sharded op (local partial kernel, one all_reduce,
-local finishing kernel) and compares with the oracle on the whole input.
+local finishing kernel) and compares with the oracle on the whole input —
+once with NCCL's all_reduce and once with the library's own all-reduce
+kernel over peer memory (kbb200.p2p.PeerComm, CUDA IPC).
 Skipped unless the process sees at least 2 GPUs.  NVLS is switched off (plain
 NCCL rings over NVLink).
 """
@@ -57,6 +59,7 @@ def _worker(rank, world, port, q):
         got = dist.frobenius_normalize(dist.shard(x, rank, world).to(dev)).cpu().numpy()
         lo, hi = dist.shard_range(8, rank, world)
         res["frobenius"] = (got, O.frobenius_normalize(x.numpy())[lo:hi], 1e-5)
+        x0, lo0, hi0 = x, lo, hi
 
         x = torch.randn(6, 32, 20, 24, generator=g) * 2 + 1
         w, bb = 1 + 0.02 * torch.randn(32, generator=g), 0.02 * torch.randn(32, generator=g)
@@ -65,9 +68,44 @@ def _worker(rank, world, port, q):
         res["batchnorm"] = (got, O.batch_norm_train(x.numpy(), w.numpy(), bb.numpy())[lo:hi], 1e-5)
 
         A, B = torch.randn(256, 65536, generator=g), torch.randn(65536, 256, generator=g)
-        got = dist.matmul_splitk(dist.shard(A, rank, world, dim=1).contiguous().to(dev),
-                                 dist.shard(B, rank, world, dim=0).contiguous().to(dev)).cpu().numpy()
-        res["splitk"] = (got, O.matmul(A.numpy(), B.numpy()), 1e-3)
+        As = dist.shard(A, rank, world, dim=1).contiguous().to(dev)
+        Bs = dist.shard(B, rank, world, dim=0).contiguous().to(dev)
+        got = dist.matmul_splitk(As, Bs).cpu().numpy()
+        want_c = O.matmul(A.numpy(), B.numpy())
+        res["splitk"] = (got, want_c, 1e-3)
+
+        lg = torch.randn(1000, 500, generator=g) * 2
+        tg = torch.randint(0, 500, (1000,), generator=g)
+        tg[[3, 700]] = -100
+        lgs, tgs = dist.shard(lg, rank, world).to(dev), dist.shard(tg, rank, world).to(dev)
+        got = dist.cross_entropy(lgs, tgs)
+        want_ce = float(O.cross_entropy(lg.numpy(), tg.numpy()))
+        res["cross_entropy"] = (float(got), want_ce, 1e-5)
+
+        # the same ops over the library's peer-memory all-reduce (CUDA IPC)
+        from kbb200.p2p import PeerComm
+
+        comm = PeerComm(slot_bytes=1 << 20, timeout_s=5.0)
+        try:
+            sa, sb = dist.shard(a, rank, world).to(dev), dist.shard(b, rank, world).to(dev)
+            for rep in range(3):  # several epochs: both slots, reuse
+                got = dist.mse_loss(sa, sb, total_n=a.numel(), comm=comm)
+                res[f"p2p_mse{rep}"] = (float(got), float(O.mse_loss(a.numpy(), b.numpy())), 1e-3)
+            got = dist.frobenius_normalize(dist.shard(x0, rank, world).to(dev), comm=comm).cpu().numpy()
+            res["p2p_frobenius"] = (got, O.frobenius_normalize(x0.numpy())[lo0:hi0], 1e-5)
+            got = dist.cross_entropy(lgs, tgs, comm=comm)
+            res["p2p_cross_entropy"] = (float(got), want_ce, 1e-5)
+            c1 = dist.matmul_splitk(As, Bs, comm=comm)
+            c2 = dist.matmul_splitk(As, Bs, comm=comm)
+            res["p2p_splitk"] = (c1.cpu().numpy(), want_c, 1e-3)
+            res["p2p_splitk_deterministic"] = (float(torch.equal(c1, c2)), 1.0, 0.0)
+            # every rank holds the same bits (rank-ordered sum)
+            gathered = [torch.empty_like(c1) for _ in range(world)]
+            tdist.all_gather(gathered, c1)
+            res["p2p_splitk_replicated"] = (float(all(torch.equal(gathered[0], t) for t in gathered)), 1.0, 0.0)
+            comm.check()
+        finally:
+            comm.close()
         torch.cuda.synchronize()
         tdist.destroy_process_group()
         q.put((rank, "ok", res))
