@@ -473,7 +473,7 @@ def _main(sink) -> int:
         if a.collective == "p2p":
             from kbb200.p2p import PeerComm
 
-            comm = PeerComm(slot_bytes=1 << 20, timeout_s=10.0, device=device)
+            comm = PeerComm(payload_bytes=1 << 20, timeout_s=10.0, device=device)
     peaks = load_peaks()
     runners = []
     for n in ops:

@@ -259,9 +259,11 @@ KB_API int kb_cross_entropy_finalize_f32(const double* total, float* out, kbStre
  * one GPU and has no collective; these entries replace the NCCL all_reduce
  * between each partial entry and its finish entry with one cooperative
  * kernel over peer memory (CUDA IPC over NVLink, no multicast):
- *   buffer   kb_p2p_buffer_alloc(kb_p2p_buffer_bytes(slot), &p) on every rank
- *            (zeroed); kb_p2p_ipc_handle / kb_p2p_ipc_open share it; `bufs`
- *            is a DEVICE array of the world base pointers (own at [rank]).
+ *   buffer   kb_p2p_buffer_alloc(kb_p2p_buffer_bytes(payload, world), &p) on
+ *            every rank (zeroed); kb_p2p_ipc_handle / kb_p2p_ipc_open share
+ *            it; `bufs` is a DEVICE array of the world base pointers (own at
+ *            [rank]).  Each rank pushes its contribution into every rank's
+ *            buffer, so payload bytes per call <= the `payload` given here.
  *   call     every rank makes the same calls in the same order with the
  *            same epoch, starting at 1 and increasing by 1 per call;
  *            dst = sum over ranks of src (rank order: bit-identical on all
@@ -270,7 +272,7 @@ KB_API int kb_cross_entropy_finalize_f32(const double* total, float* out, kbStre
  *            the fault word (kb_p2p_read_fault) and leaves dst unwritten;
  *            the buffer set must then be discarded.                       */
 KB_API size_t kb_p2p_header_bytes(void);
-KB_API size_t kb_p2p_buffer_bytes(size_t slot_bytes);
+KB_API size_t kb_p2p_buffer_bytes(size_t payload_bytes, int world);
 KB_API int kb_p2p_buffer_alloc(size_t bytes, void** ptr);
 KB_API int kb_p2p_buffer_free(void* ptr);
 KB_API int kb_p2p_ipc_handle(void* ptr, void* handle /* 64 bytes */);

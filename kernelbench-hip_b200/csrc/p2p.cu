@@ -4,25 +4,26 @@
 //
 // Each rank owns one symmetric buffer (same size on every rank, cudaMalloc'd
 // here, zeroed once), opened by the peers through CUDA IPC (peer access over
-// NVLink; no multicast objects, no NVLS).  Layout:
-//   [0, 4 KiB)        header: flags[2][kMaxRanks] (epoch at which rank p's
-//                     data slot was complete, written by p into every
-//                     rank's header), grid-barrier count and generation
-//   [4 KiB, +cap)     data slot 0
-//   [.., +cap)        data slot 1
-// A call with epoch e uses slot e & 1 and runs as one cooperative kernel
-// (all CTAs co-resident):
-//   1. write this rank's contribution into its own slot (for split-K: the
-//      fixed-order sum of its K-split partial tiles);
-//   2. grid barrier (bounded wait);
-//   3. CTA 0 publishes: system-scope release store of e into flags[slot][rank]
+// NVLink; no multicast objects, no NVLS).  Layout, with cap bytes per rank:
+//   [0, 4 KiB)                 header: flags[2][kMaxRanks] (flags[s][p] = the
+//                              epoch at which rank p's data for slot s
+//                              arrived here, written by p), grid-barrier
+//                              count and generation
+//   [4 KiB + (s * world + p) * cap, + cap)   slot s, data pushed by rank p
+// A call with epoch e uses slot s = e & 1 and runs as one kernel
+// (cooperative when it has more than one CTA, so all CTAs are co-resident):
+//   1. push: this rank's contribution (for split-K: the fixed-order sum of
+//      its K-split partial tiles) is stored into slot s, part `rank`, of
+//      every rank's buffer — posted writes over NVLink;
+//   2. system-scope fence, then a grid barrier (bounded wait);
+//   3. CTA 0 publishes: system-scope release store of e into flags[s][rank]
 //      of every rank;
-//   4. every CTA waits (bounded) until flags[slot][p] == e for every p;
-//   5. dst[i] = sum over p = 0 .. world-1 of slot_p[i], in rank order: every
-//      rank computes bit-identical results.
-// Slot reuse is safe: rank p rewrites slot e & 1 only in call e + 2, after
-// its call e + 1 saw every rank's signal, which each rank sends only after
-// its call e (and so its reads of slot e & 1) completed.
+//   4. every CTA waits (bounded) until its own flags[s][p] == e for every p;
+//   5. dst[i] = sum over p = 0 .. world-1 of part p of its own slot s, in
+//      rank order (local reads): every rank computes bit-identical results.
+// Slot reuse is safe: rank q writes part q of slot e & 1 again only in call
+// e + 2, after its call e + 1 saw every rank's signal, which each rank sends
+// only after its call e (and so its reads of slot e & 1) completed.
 // Every wait is bounded by %globaltimer; on expiry the kernel records a
 // fault word (kb_p2p_read_fault), leaves without writing dst, and the buffer
 // set must be discarded (its barrier state is no longer consistent).
@@ -50,7 +51,7 @@ static_assert(sizeof(Header) <= kHeaderBytes, "header");
 struct P2PArgs {
   char* const* bufs;   // device array [world]: base of every rank's buffer (own at [rank])
   int rank, world;
-  size_t cap;          // bytes per data slot
+  size_t cap;          // bytes per rank part of a slot
   int64_t n;           // elements
   const void* src;     // mode 0: n elements; mode 1: `splits` fp32 partials of n, stride n
   int splits;
@@ -99,34 +100,41 @@ __device__ __forceinline__ T load_cv(const T* p) {
   return __ldcv(p);
 }
 
+// offset of part p of slot s
+__device__ __forceinline__ size_t part_off(unsigned s, int p, int world, size_t cap) {
+  return kHeaderBytes + ((size_t)s * world + p) * cap;
+}
+
 template <class T, int MODE>
 __global__ void __launch_bounds__(kP2PThreads) p2p_allreduce_kernel(P2PArgs a) {
   __shared__ int s_ok;
   const unsigned slot = a.epoch & 1u;
   Header* mine_h = reinterpret_cast<Header*>(a.bufs[a.rank]);
-  T* mine = reinterpret_cast<T*>(a.bufs[a.rank] + kHeaderBytes + slot * a.cap);
   const int64_t stride = (int64_t)gridDim.x * blockDim.x;
   const int64_t i0 = (int64_t)blockIdx.x * blockDim.x + threadIdx.x;
+  const size_t my_part = part_off(slot, a.rank, a.world, a.cap);
 
-  // 1. this rank's contribution
-  if (MODE == 0) {
-    const T* src = static_cast<const T*>(a.src);
-    for (int64_t i = i0; i < a.n; i += stride) mine[i] = src[i];
-  } else {
-    const float* part = static_cast<const float*>(a.src);
-    for (int64_t i = i0; i < a.n; i += stride) {
+  // 1. push this rank's contribution into part `rank` of every rank's slot
+  for (int64_t i = i0; i < a.n; i += stride) {
+    T v;
+    if (MODE == 0) {
+      v = static_cast<const T*>(a.src)[i];
+    } else {
+      const float* part = static_cast<const float*>(a.src);
       float s = 0.f;
 #pragma unroll 8
       for (int z = 0; z < a.splits; ++z) s += part[(int64_t)z * a.n + i];  // split order; loads run ahead
-      mine[i] = s;
+      v = s;
     }
+    for (int p = 0; p < a.world; ++p) reinterpret_cast<T*>(a.bufs[p] + my_part)[i] = v;
   }
 
-  // 2. grid barrier (all CTAs are co-resident: cooperative launch)
+  // 2. the pushes are visible system-wide, then a grid barrier
+  __threadfence_system();
   __syncthreads();
   if (threadIdx.x == 0) {
-    __threadfence();
     bool ok = true;
+    if (gridDim.x > 1) {
     const unsigned old = atomicAdd(&mine_h->bar_count, 1u);
     if (old == gridDim.x - 1) {
       mine_h->bar_count = 0;
@@ -136,7 +144,8 @@ __global__ void __launch_bounds__(kP2PThreads) p2p_allreduce_kernel(P2PArgs a) {
       ok = bounded_wait([&] { return load_volatile(&mine_h->bar_gen) == a.epoch; }, a.timeout_ns,
                         (1 << 8) | a.rank);
     }
-    // 3. publish this rank's slot to every rank
+    }
+    // 3. tell every rank that this rank's part has arrived
     if (ok && blockIdx.x == 0) {
       __threadfence_system();
       for (int p = 0; p < a.world; ++p) {
@@ -154,12 +163,13 @@ __global__ void __launch_bounds__(kP2PThreads) p2p_allreduce_kernel(P2PArgs a) {
   if (!s_ok) return;
   __threadfence_system();
 
-  // 5. rank-ordered sum of every rank's slot
+  // 5. rank-ordered sum of the parts that arrived in this rank's slot
   T* dst = static_cast<T*>(a.dst);
+  const char* own = a.bufs[a.rank];
   for (int64_t i = i0; i < a.n; i += stride) {
     T acc = T(0);
     for (int p = 0; p < a.world; ++p)
-      acc += load_cv(reinterpret_cast<const T*>(a.bufs[p] + kHeaderBytes + slot * a.cap) + i);
+      acc += load_cv(reinterpret_cast<const T*>(own + part_off(slot, p, a.world, a.cap)) + i);
     dst[i] = acc;
   }
 }
@@ -182,13 +192,18 @@ int launch_p2p(const char* name, P2PArgs a, cudaStream_t s) {
   // each), capped at what is co-resident
   const int64_t want = std::max<int64_t>(1, ceil_div(a.n, (int64_t)kP2PThreads));
   const int grid = (int)std::min<int64_t>(want, (int64_t)sm_count() * per_sm);
+  if (grid == 1) {  // one CTA: no grid barrier, an ordinary launch
+    kern<<<1, kP2PThreads, 0, s>>>(a);
+    return check_launch(name);
+  }
   void* args[] = {&a};
   KB_CUDA(cudaLaunchCooperativeKernel((const void*)kern, dim3(grid), dim3(kP2PThreads), args, 0, s));
   return KB_OK;
 }
 
-size_t slot_cap(size_t buf_bytes) {
-  return buf_bytes > kHeaderBytes ? ((buf_bytes - kHeaderBytes) / 2) & ~(size_t)255 : 0;
+// bytes per rank part of a slot of a buffer of buf_bytes
+size_t part_cap(size_t buf_bytes, int world) {
+  return buf_bytes > kHeaderBytes && world > 0 ? ((buf_bytes - kHeaderBytes) / 2 / world) & ~(size_t)255 : 0;
 }
 
 }  // namespace
@@ -198,8 +213,8 @@ extern "C" {
 
 size_t kb_p2p_header_bytes(void) { return kb::kHeaderBytes; }
 
-size_t kb_p2p_buffer_bytes(size_t slot_bytes) {
-  return kb::kHeaderBytes + 2 * ((slot_bytes + 255) & ~(size_t)255);
+size_t kb_p2p_buffer_bytes(size_t payload_bytes, int world) {
+  return kb::kHeaderBytes + 2 * (size_t)(world > 0 ? world : 1) * ((payload_bytes + 255) & ~(size_t)255);
 }
 
 int kb_p2p_buffer_alloc(size_t bytes, void** ptr) {
@@ -254,14 +269,14 @@ int kb_p2p_read_fault(int clear, int* value) {
 
 int kb_p2p_allreduce_f64(void* const* bufs, int rank, int world, size_t buf_bytes, const double* src,
                          double* dst, int64_t n, unsigned epoch, uint64_t timeout_ns, kbStream stream) {
-  kb::P2PArgs a{reinterpret_cast<char* const*>(bufs), rank, world, kb::slot_cap(buf_bytes), n, src, 0, dst,
+  kb::P2PArgs a{reinterpret_cast<char* const*>(bufs), rank, world, kb::part_cap(buf_bytes, world), n, src, 0, dst,
                 epoch, timeout_ns};
   return kb::launch_p2p<double, 0>("kb_p2p_allreduce_f64", a, stream);
 }
 
 int kb_p2p_allreduce_f32(void* const* bufs, int rank, int world, size_t buf_bytes, const float* src,
                          float* dst, int64_t n, unsigned epoch, uint64_t timeout_ns, kbStream stream) {
-  kb::P2PArgs a{reinterpret_cast<char* const*>(bufs), rank, world, kb::slot_cap(buf_bytes), n, src, 0, dst,
+  kb::P2PArgs a{reinterpret_cast<char* const*>(bufs), rank, world, kb::part_cap(buf_bytes, world), n, src, 0, dst,
                 epoch, timeout_ns};
   return kb::launch_p2p<float, 0>("kb_p2p_allreduce_f32", a, stream);
 }
@@ -270,7 +285,7 @@ int kb_p2p_splitk_allreduce_f32(void* const* bufs, int rank, int world, size_t b
                                 int splits, float* dst, int64_t n, unsigned epoch, uint64_t timeout_ns,
                                 kbStream stream) {
   KB_REQUIRE(splits >= 1, KB_ERR_INVALID_ARG, "kb_p2p_splitk_allreduce_f32: splits < 1");
-  kb::P2PArgs a{reinterpret_cast<char* const*>(bufs), rank, world, kb::slot_cap(buf_bytes), n, partials,
+  kb::P2PArgs a{reinterpret_cast<char* const*>(bufs), rank, world, kb::part_cap(buf_bytes, world), n, partials,
                 splits, dst, epoch, timeout_ns};
   return kb::launch_p2p<float, 1>("kb_p2p_splitk_allreduce_f32", a, stream);
 }

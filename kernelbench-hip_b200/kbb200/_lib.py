@@ -66,7 +66,7 @@ SIGNATURES: dict[str, tuple] = {
     "kb_cross_entropy_partial_f64": (_int, [_p, _p, _p, _i64, _i64, _i64, _p, _sz, _p]),
     "kb_cross_entropy_finalize_f32": (_int, [_p, _p, _p]),
     "kb_p2p_header_bytes": (_sz, []),
-    "kb_p2p_buffer_bytes": (_sz, [_sz]),
+    "kb_p2p_buffer_bytes": (_sz, [_sz, _int]),
     "kb_p2p_buffer_alloc": (_int, [_sz, C.POINTER(C.c_void_p)]),
     "kb_p2p_buffer_free": (_int, [_p]),
     "kb_p2p_ipc_handle": (_int, [_p, _p]),

@@ -507,4 +507,5 @@ def matmul_splitk_partials(A, B):
     sp = C.c_int(1)
     check(fn, LIB.kb_gemm_splitk_partials_3xtf32(A.data_ptr(), B.data_ptr(), M, N, K, ws.data_ptr(),
                                                  ws.numel(), C.byref(sp), _stream(A)))
-    return ws, sp.value
+    splits = sp.value
+    return ws.view(torch.float32)[: splits * M * N].view(splits, M, N), splits

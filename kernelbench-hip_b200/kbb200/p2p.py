@@ -5,8 +5,9 @@ exchange one small partial per rank.  `PeerComm` replaces the NCCL
 all_reduce there with the library's own cooperative kernel over peer memory
 (include/kbb200.h, kb_p2p_*): every rank allocates one symmetric buffer,
 the buffers are shared through CUDA IPC handles (exchanged once with
-torch.distributed), and each call signals the peers with system-scope flags
-and sums all ranks' slots in rank order — identical bits on every rank.
+torch.distributed), and each call pushes this rank's contribution into every
+rank's buffer, raises a system-scope flag on each, waits for the peers' flags
+and sums the parts that arrived in rank order — identical bits on every rank.
 Plain peer loads and stores over NVLink: no multicast objects.
 
 Every rank must make the same calls in the same order.  A wait that runs
@@ -24,14 +25,14 @@ from ._lib import LIB, KbError, check
 
 
 class PeerComm:
-    def __init__(self, group=None, slot_bytes: int = 1 << 20, timeout_s: float = 2.0, device=None):
+    def __init__(self, group=None, payload_bytes: int = 1 << 20, timeout_s: float = 2.0, device=None):
         self.group = group
         self.rank = tdist.get_rank(group)
         self.world = tdist.get_world_size(group)
         self.device = torch.device(device) if device is not None else torch.device(
             "cuda", torch.cuda.current_device())
-        self.slot_bytes = int(slot_bytes)
-        self.buf_bytes = LIB.kb_p2p_buffer_bytes(self.slot_bytes)
+        self.payload_bytes = int(payload_bytes)  # largest all-reduce of one call
+        self.buf_bytes = LIB.kb_p2p_buffer_bytes(self.payload_bytes, self.world)
         self.timeout_ns = int(timeout_s * 1e9)
         self.epoch = 0
         self._own = C.c_void_p()

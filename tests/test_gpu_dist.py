@@ -85,7 +85,7 @@ def _worker(rank, world, port, q):
         # the same ops over the library's peer-memory all-reduce (CUDA IPC)
         from kbb200.p2p import PeerComm
 
-        comm = PeerComm(slot_bytes=1 << 20, timeout_s=5.0)
+        comm = PeerComm(payload_bytes=1 << 20, timeout_s=5.0)
         try:
             sa, sb = dist.shard(a, rank, world).to(dev), dist.shard(b, rank, world).to(dev)
             for rep in range(3):  # several epochs: both slots, reuse

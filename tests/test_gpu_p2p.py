@@ -1,9 +1,9 @@
 """GPU, one device: the peer-memory all-reduce kernel (kb_p2p_*) with a
 second rank emulated on the host.
 
-The "peer" buffer is a second symmetric buffer on the same GPU; its data slot
-and its ready flag in our header are written by the host before the launch,
-so no kernel waits for another kernel.  Checked: the rank-ordered sum
+The "peer" buffer is a second symmetric buffer on the same GPU; the data the
+peer would push into our buffer and its ready flag in our header are written
+by the host before the launch, so no kernel waits for another kernel.  Checked: the rank-ordered sum
 (float32, float64, in place), the fused split-K form, slot alternation over
 epochs, and a wait that runs out (a peer flag that nothing sets) — the
 kernel reports it in the fault word and leaves dst untouched.  The real
@@ -24,13 +24,14 @@ MAX_RANKS = 64  # flags[2][64] uint32 at byte 0 of each buffer (csrc/p2p.cu)
 class Emulated:
     """Rank 0 of a world of 2 whose rank 1 is played by the host."""
 
-    def __init__(self, device, slot_bytes=1 << 16):
+    def __init__(self, device, payload_bytes=1 << 16):
         from kbb200._lib import LIB, check
 
         self.LIB, self.check = LIB, check
-        self.buf_bytes = LIB.kb_p2p_buffer_bytes(slot_bytes)
+        self.world = 2
+        self.buf_bytes = LIB.kb_p2p_buffer_bytes(payload_bytes, self.world)
         self.hdr = LIB.kb_p2p_header_bytes()
-        self.cap = ((self.buf_bytes - self.hdr) // 2) & ~255
+        self.cap = ((self.buf_bytes - self.hdr) // 2 // self.world) & ~255  # bytes per rank part
         self.ptrs = []
         for _ in range(2):
             p = C.c_void_p()
@@ -51,8 +52,9 @@ class Emulated:
         torch.cuda.synchronize()
 
     def set_peer(self, epoch: int, data: torch.Tensor) -> None:
+        """What rank 1 would push into our buffer (part 1 of slot epoch & 1)."""
         slot = epoch & 1
-        self.write(self.ptrs[1] + self.hdr + slot * self.cap, data)
+        self.write(self.ptrs[0] + self.hdr + (slot * self.world + 1) * self.cap, data)
         flag = torch.tensor([epoch], dtype=torch.int32, device=self.device)
         self.write(self.ptrs[0] + (slot * MAX_RANKS + 1) * 4, flag)
 
