@@ -51,7 +51,7 @@ FLUSH_BYTES = 256 * 1024 * 1024
 # kernels launched per op call (for gpu_launches)
 LAUNCHES = {"gelu_tanh": 1, "gelu_erf": 1, "swish": 1, "relu": 1, "layer_norm": 1, "rms_norm": 1,
             "softmax": 1, "log_softmax": 1, "sum_dim": 1, "mean_dim": 1, "argmax_dim": 1,
-            "mse_loss": 2, "frobenius_normalize": 2, "max_pool2d": 1, "batch_norm_train": 2,
+            "mse_loss": 2, "frobenius_normalize": 3, "max_pool2d": 1, "batch_norm_train": 2,
             "matmul": 1, "bmm": 1, "matmul_splitk": 2, "gemv": 1, "matmul_transposed_a": 1,
             "matmul_symmetric": 1, "diag_matmul": 1, "matmul_small_k": 1,
             "avg_pool2d": 1, "cumsum": 1, "cross_entropy": 2}

@@ -10,9 +10,11 @@
 // promoted to fp64.
 //
 // Frobenius needs the global norm before any output can be written and the
-// input (1 GiB) does not fit on chip, so x is read twice.  The scale pass
-// walks the tensor from the end backwards so that its first tiles are the
-// ones the sum pass touched last, which are still resident in the 126 MB L2.
+// input (1 GiB) does not fit on chip, so x is read twice: the sum pass, a
+// one-CTA finish that writes the fp64 total, and the scale pass (one
+// 4096-float tile per CTA, 256-bit accesses), which walks the tensor from the
+// end backwards so that its first tiles are the ones the sum pass touched
+// last, still resident in the 126 MB L2.
 #include "kb_common.cuh"
 
 namespace kb {
@@ -109,42 +111,71 @@ __global__ void mse_finalize_kernel(const double* __restrict__ total, float* out
   out[0] = (float)(total[0] / denom);
 }
 
-// y = x / sqrt(sumsq), walking tiles from the end of the tensor backwards.
-// sumsq comes either from `count` partials (single GPU) or from one fp64
-// total (sharded: count == 0).
+// y = x / sqrt(sumsq) with sumsq one fp64 total.  One 4096-float tile per
+// CTA, all of a thread's loads issued before its stores, tiles taken from
+// the end of the tensor backwards (CTAs start in blockIdx order, so the
+// first tiles are the ones the sum pass read last, still in L2).
+constexpr int kScaleTile = 4096;
+
+__device__ __forceinline__ float inv_norm_source(const double* sumsq) { return (float)sqrt(*sumsq); }
+
+template <int W>
 __global__ void __launch_bounds__(kThreads)
-scale_kernel(const float* __restrict__ x, float* __restrict__ y, int64_t n, bool vec,
-             const double* __restrict__ partials, int count) {
-  __shared__ double red[32];
-  const double ss = count > 0 ? sum_partials(partials, count, red) : partials[0];
-  const float norm = (float)sqrt(ss);
-  int64_t scalar_begin = 0;
-  if (vec) {
-    const int64_t nvec = n / 4;
-    const float4* x4 = reinterpret_cast<const float4*>(x);
-    float4* y4 = reinterpret_cast<float4*>(y);
-    const int64_t tile = (int64_t)kThreads * kUnroll;
-    const int64_t ntiles = nvec / tile;
-    for (int64_t i = ntiles * tile + (int64_t)blockIdx.x * kThreads + threadIdx.x; i < nvec;
-         i += (int64_t)gridDim.x * kThreads) {
-      const float4 v = __ldg(x4 + i);
-      st_stream(y4 + i, make_float4(v.x / norm, v.y / norm, v.z / norm, v.w / norm));
-    }
-    for (int64_t t = ntiles - 1 - blockIdx.x; t >= 0; t -= gridDim.x) {
-      const int64_t base = t * tile + threadIdx.x;
-      float4 v[kUnroll];
+scale_tile_kernel(const float* __restrict__ x, float* __restrict__ y, int64_t tiles,
+                  const double* __restrict__ sumsq) {
+  constexpr int U = kScaleTile / (kThreads * W);
+  const float norm = inv_norm_source(sumsq);
+  const int64_t base = (tiles - 1 - (int64_t)blockIdx.x) * kScaleTile + threadIdx.x * W;
+  f32x8 v[U];
 #pragma unroll
-      for (int u = 0; u < kUnroll; ++u) v[u] = ld_stream(x4 + base + u * kThreads);
-#pragma unroll
-      for (int u = 0; u < kUnroll; ++u)
-        st_stream(y4 + base + u * kThreads,
-                  make_float4(v[u].x / norm, v[u].y / norm, v[u].z / norm, v[u].w / norm));
+  for (int u = 0; u < U; ++u) {
+    if (W == 8) {
+      v[u] = ld_stream8(x + base + u * kThreads * W);
+    } else {
+      const float4 q = ld_stream(reinterpret_cast<const float4*>(x + base + u * kThreads * W));
+      v[u].v[0] = q.x;
+      v[u].v[1] = q.y;
+      v[u].v[2] = q.z;
+      v[u].v[3] = q.w;
     }
-    scalar_begin = nvec * 4;
   }
-  for (int64_t i = scalar_begin + (int64_t)blockIdx.x * kThreads + threadIdx.x; i < n;
+#pragma unroll
+  for (int u = 0; u < U; ++u) {
+#pragma unroll
+    for (int k = 0; k < W; ++k) v[u].v[k] = v[u].v[k] / norm;
+    if (W == 8)
+      st_stream8(y + base + u * kThreads * W, v[u]);
+    else
+      st_stream(reinterpret_cast<float4*>(y + base + u * kThreads * W),
+                make_float4(v[u].v[0], v[u].v[1], v[u].v[2], v[u].v[3]));
+  }
+}
+
+__global__ void __launch_bounds__(kThreads)
+scale_scalar_kernel(const float* __restrict__ x, float* __restrict__ y, int64_t begin, int64_t n,
+                    const double* __restrict__ sumsq) {
+  const float norm = inv_norm_source(sumsq);
+  for (int64_t i = begin + (int64_t)blockIdx.x * kThreads + threadIdx.x; i < n;
        i += (int64_t)gridDim.x * kThreads)
     y[i] = x[i] / norm;
+}
+
+int launch_scale(const char* name, const float* x, float* y, int64_t n, const double* sumsq, cudaStream_t s) {
+  const int64_t tiles = n / kScaleTile;
+  KB_REQUIRE(tiles <= 0x7fffffff, KB_ERR_UNSUPPORTED, "%s: too large", name);
+  int64_t done = 0;
+  if (tiles > 0 && aligned32(x) && aligned32(y)) {
+    scale_tile_kernel<8><<<(unsigned)tiles, kThreads, 0, s>>>(x, y, tiles, sumsq);
+    done = tiles * kScaleTile;
+  } else if (tiles > 0 && aligned16(x) && aligned16(y)) {
+    scale_tile_kernel<4><<<(unsigned)tiles, kThreads, 0, s>>>(x, y, tiles, sumsq);
+    done = tiles * kScaleTile;
+  }
+  if (done < n) {
+    const int grid = (int)std::max<int64_t>(1, std::min<int64_t>(ceil_div(n - done, kThreads), (int64_t)sm_count() * 8));
+    scale_scalar_kernel<<<grid, kThreads, 0, s>>>(x, y, done, n, sumsq);
+  }
+  return check_launch(name);
 }
 
 int check_ws(const char* name, void* ws, size_t bytes, size_t need) {
@@ -210,7 +241,8 @@ int kb_mse_finalize_f32(const double* total, float* out, int64_t total_n, kbStre
   return kb::check_launch("kb_mse_finalize_f32");
 }
 
-size_t kb_frobenius_workspace_size(int64_t) { return kb::kMaxPartials * sizeof(double); }
+// the partials, then the fp64 total
+size_t kb_frobenius_workspace_size(int64_t) { return (kb::kMaxPartials + 2) * sizeof(double); }
 
 int kb_frobenius_normalize_f32(const float* x, float* y, int64_t n, void* workspace,
                                size_t workspace_bytes, kbStream stream) {
@@ -220,12 +252,12 @@ int kb_frobenius_normalize_f32(const float* x, float* y, int64_t n, void* worksp
   KB_REQUIRE(x && y, KB_ERR_INVALID_ARG, "%s: null pointer", name);
   if (int st = kb::check_ws(name, workspace, workspace_bytes, kb_frobenius_workspace_size(n))) return st;
   double* parts = static_cast<double*>(workspace);
+  double* total = parts + kb::kMaxPartials;
   int count = 0;
   if (int st = kb::launch_partials(name, x, nullptr, n, parts, stream, &count)) return st;
-  const bool vec = kb::aligned16(x) && kb::aligned16(y);
-  const int grid = kb::reduce_grid(vec ? n / 4 : n);
-  kb::scale_kernel<<<grid, kb::kThreads, 0, stream>>>(x, y, n, vec, parts, count);
-  return kb::check_launch(name);
+  kb::finish_kernel<<<1, kb::kThreads, 0, stream>>>(parts, count, 1.0, nullptr, total);
+  if (int st = kb::check_launch(name)) return st;
+  return kb::launch_scale(name, x, y, n, total, stream);
 }
 
 int kb_sumsq_partial_f64(const float* x, double* sumsq, int64_t n, void* workspace,
@@ -249,10 +281,7 @@ int kb_scale_by_inv_norm_f32(const float* x, float* y, int64_t n, const double* 
   KB_REQUIRE(n >= 0, KB_ERR_INVALID_ARG, "%s: negative n", name);
   if (n == 0) return KB_OK;
   KB_REQUIRE(x && y && total_sumsq, KB_ERR_INVALID_ARG, "%s: null pointer", name);
-  const bool vec = kb::aligned16(x) && kb::aligned16(y);
-  const int grid = kb::reduce_grid(vec ? n / 4 : n);
-  kb::scale_kernel<<<grid, kb::kThreads, 0, stream>>>(x, y, n, vec, total_sumsq, 0);
-  return kb::check_launch(name);
+  return kb::launch_scale(name, x, y, n, total_sumsq, stream);
 }
 
 }  // extern "C"
