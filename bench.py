@@ -18,7 +18,9 @@ this family), and the step time is the max over ranks.
 
 One JSON line is printed by rank 0.  `value` is GB/s of algorithmic bytes
 over device time; `e2e` repeats the step through the public candidate API
-with pinned host inputs and outputs (H2D + kernels + D2H timed); `roofline`
+with pinned host inputs and outputs (H2D + kernels + D2H timed; ops whose
+rows are independent stream through in row blocks, copies in both
+directions overlapping the kernels on three streams); `roofline`
 covers the dominant kernel; `cpu_baseline` is the torch-eager CPU reference
 on a bounded sample.
 """
@@ -277,16 +279,72 @@ def load_candidate(problem: str):
     return mod
 
 
-def e2e_runner(problem: str, host_inputs: list, host_out: torch.Tensor, device):
+# inputs split along dim 0 when an op's rows (batch items) are independent;
+# the output splits along dim 0 with them, other inputs are copied whole
+ROW_SPLIT = {"gelu_tanh": (0,), "gelu_erf": (0,), "swish": (0,), "relu": (0,), "layer_norm": (0,),
+             "rms_norm": (0,), "softmax": (0,), "log_softmax": (0,), "sum_dim": (0,), "mean_dim": (0,),
+             "argmax_dim": (0,), "max_pool2d": (0,), "avg_pool2d": (0,), "cumsum": (0,), "bmm": (0, 1),
+             "gemv": (0,), "diag_matmul": (0, 1), "matmul": (0,), "matmul_symmetric": (0,),
+             "matmul_small_k": (0,)}
+
+
+class E2EStreams:
+    """The three streams the end-to-end step runs on (host-to-device copies,
+    candidate forwards, device-to-host copies), shared by every op of the
+    step so that one op's uploads overlap the previous op's tail."""
+
+    def __init__(self, device):
+        self.device = device
+        self.s_in, self.s_cmp, self.s_out = (torch.cuda.Stream(device) for _ in range(3))
+
+    def begin(self):  # work already on the current stream comes first
+        self.s_in.wait_stream(torch.cuda.current_stream(self.device))
+
+    def end(self):  # the current stream waits for every download
+        torch.cuda.current_stream(self.device).wait_stream(self.s_out)
+
+
+def e2e_runner(name: str, problem: str, host_inputs: list, host_out: torch.Tensor, device, chunks: int,
+               streams: E2EStreams):
     """One end-to-end call through the candidate API: pinned host inputs ->
-    device, Model.forward (the compiled EXT entry), result -> pinned host."""
+    device, Model.forward (the compiled EXT entry), result -> pinned host.
+    Row-independent ops are cut into `chunks` row blocks whose host-to-device
+    copy, forward and device-to-host copy run on the three streams, so the two
+    copy directions and the kernels overlap; other ops run whole.  A block's
+    device input is rewritten (next call) only after its forward finished."""
     model = load_candidate(problem).Model().to(device)
+    split = ROW_SPLIT.get(name) if chunks > 1 else None
+    rows = host_inputs[0].shape[0] if host_inputs[0].dim() else 1
+    k = min(chunks, rows) if split else 1
+    bounds = [(rows * i // k, rows * (i + 1) // k) for i in range(k)]
+    dev_in = [torch.empty(h.shape, dtype=h.dtype, device=device) for h in host_inputs]
+    st = streams
+    done = [None] * k  # forward of block i finished (previous call)
 
     def run():
-        d = [h.to(device, non_blocking=True) for h in host_inputs]
-        with torch.no_grad():
-            out = model(*d)
-        host_out.copy_(out.reshape(host_out.shape), non_blocking=True)
+        for ci, (lo, hi) in enumerate(bounds):
+            if done[ci] is not None:
+                st.s_in.wait_event(done[ci])
+            if ci == 0 and done[k - 1] is not None:  # whole inputs are read by every block
+                st.s_in.wait_event(done[k - 1])
+            with torch.cuda.stream(st.s_in):
+                for j, h in enumerate(host_inputs):
+                    if split and j in split:
+                        dev_in[j][lo:hi].copy_(h[lo:hi], non_blocking=True)
+                    elif ci == 0:
+                        dev_in[j].copy_(h, non_blocking=True)
+                ev_in = torch.cuda.Event()
+                ev_in.record(st.s_in)
+            st.s_cmp.wait_event(ev_in)
+            with torch.cuda.stream(st.s_cmp), torch.no_grad():
+                out = model(*[d[lo:hi] if (split and j in split) else d for j, d in enumerate(dev_in)])
+                done[ci] = torch.cuda.Event()
+                done[ci].record(st.s_cmp)
+            st.s_out.wait_event(done[ci])
+            out.record_stream(st.s_out)
+            with torch.cuda.stream(st.s_out):
+                dst = host_out[lo:hi] if split else host_out
+                dst.copy_(out.reshape(dst.shape), non_blocking=True)
 
     return run
 
@@ -416,6 +474,8 @@ def _main(sink) -> int:
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--cpu-steps", type=int, default=3)
     ap.add_argument("--profile-op", default=None, help="run one op 3x on a reduced input (for ncu)")
+    ap.add_argument("--e2e-chunks", type=int, default=8,
+                    help="row blocks per op in the end-to-end pipeline (1: whole op, serial)")
     ap.add_argument("--collective", choices=("p2p", "nccl"), default="p2p",
                     help="cross-GPU sum of the sharded ops: the library's peer-memory kernel or NCCL")
     ap.add_argument("--frac", type=float, default=0.25, help="input fraction for --profile-op")
@@ -562,14 +622,17 @@ def _main(sink) -> int:
     e2e = None
     if not a.no_e2e:
         e2e_fns, h2d, d2h = [], 0, 0
+        e2e_streams = E2EStreams(device)
         for n, w, ins, _, out in runners:
             hin = [t.cpu().pin_memory() for t in ins]
             hout = torch.empty(out.shape, dtype=out.dtype).pin_memory()
-            e2e_fns.append(e2e_runner(w.problem, hin, hout, device))
+            e2e_fns.append(e2e_runner(n, w.problem, hin, hout, device, a.e2e_chunks, e2e_streams))
             h2d += bytes_of(hin)
             d2h += bytes_of([hout])
+        e2e_streams.begin()
         for f in e2e_fns:
             f()
+        e2e_streams.end()
         torch.cuda.synchronize(device)
         e2e_steps = max(1, min(a.steps, 5))
         barrier()
@@ -577,9 +640,11 @@ def _main(sink) -> int:
         s0 = torch.cuda.Event(enable_timing=True)
         s1 = torch.cuda.Event(enable_timing=True)
         s0.record(stream)
+        e2e_streams.begin()
         for _ in range(e2e_steps):
             for f in e2e_fns:
                 f()
+        e2e_streams.end()
         s1.record(stream)
         torch.cuda.synchronize(device)
         e2e_ms = s0.elapsed_time(s1) / e2e_steps
@@ -589,7 +654,9 @@ def _main(sink) -> int:
             e2e_ms = t.item()
         e2e = {"value": round(step_bytes * world / (e2e_ms * 1e-3) / 1e9, 3), "unit": "GB/s",
                "h2d_bytes_per_step": h2d, "d2h_bytes_per_step": d2h, "ms_per_step": round(e2e_ms, 3),
-               "steps": e2e_steps}
+               "steps": e2e_steps,
+               "pipeline": (f"{a.e2e_chunks} row blocks per row-independent op: H2D, candidate "
+                            "Model.forward, D2H on three streams" if a.e2e_chunks > 1 else "serial")}
 
     cpu = None
     if rank == 0 and world == 1 and not a.no_cpu_baseline:
