@@ -305,8 +305,8 @@ static int cross_entropy_impl(const char* name, const float* logits, const int64
   int64_t parts;
   if (vec && classes <= 128 * 4 * 2)
     parts = kb::launch_rows<128, 2>(logits, targets, rows, classes, ignore_index, part_sum, part_count, stream);
-  else if (vec && classes <= 256 * 4 * 4)
-    parts = kb::launch_rows<256, 4>(logits, targets, rows, classes, ignore_index, part_sum, part_count, stream);
+  else if (vec && classes <= 128 * 4 * 8)  // 32 logits per thread: the block reductions amortise over more
+    parts = kb::launch_rows<128, 8>(logits, targets, rows, classes, ignore_index, part_sum, part_count, stream);
   else if (vec && classes <= 512 * 4 * 8)
     parts = kb::launch_rows<512, 8>(logits, targets, rows, classes, ignore_index, part_sum, part_count, stream);
   else {
