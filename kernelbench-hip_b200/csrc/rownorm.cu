@@ -154,7 +154,41 @@ struct ClusterReducer {
 //   v[k] holds float4 number (k * stride + lane) of this thread's segment;
 //   col4_base + k * stride + lane is its float4 index within the full row.
 // ---------------------------------------------------------------------------
-template <RowOp OP, int VPT, class R>
+// Float4 slot of a thread's k-th vector within its row segment.  PAIRED
+// puts vectors 2i and 2i+1 next to each other, so a thread's results leave
+// as one 256-bit store (fewer store instructions in flight per byte);
+// otherwise consecutive threads hold consecutive float4s.
+template <bool PAIRED>
+__device__ __forceinline__ int64_t vec_slot(int k, int lane, int stride) {
+  return PAIRED ? (int64_t)(k >> 1) * 2 * stride + 2 * lane + (k & 1) : (int64_t)k * stride + lane;
+}
+
+// writes the VPT result vectors of one thread (ok[k]: inside the row)
+template <int VPT, bool PAIRED>
+__device__ __forceinline__ void store_row(float4* yrow, const float4 (&v)[VPT], const bool (&ok)[VPT],
+                                          int lane, int stride) {
+  if constexpr (PAIRED) {
+    static_assert(VPT % 2 == 0, "paired vectors");
+#pragma unroll
+    for (int k = 0; k < VPT; k += 2) {
+      float4* dst = yrow + vec_slot<true>(k, lane, stride);
+      if (ok[k + 1]) {  // both halves inside the row (slot k+1 = slot k + 1)
+        f32x8 w;
+        w.v[0] = v[k].x; w.v[1] = v[k].y; w.v[2] = v[k].z; w.v[3] = v[k].w;
+        w.v[4] = v[k + 1].x; w.v[5] = v[k + 1].y; w.v[6] = v[k + 1].z; w.v[7] = v[k + 1].w;
+        st_stream8(reinterpret_cast<float*>(dst), w);
+      } else if (ok[k]) {
+        st_stream(dst, v[k]);
+      }
+    }
+  } else {
+#pragma unroll
+    for (int k = 0; k < VPT; ++k)
+      if (ok[k]) st_stream(yrow + vec_slot<false>(k, lane, stride), v[k]);
+  }
+}
+
+template <RowOp OP, int VPT, bool PAIRED = false, class R>
 __device__ __forceinline__ void row_math(float4 (&v)[VPT], const bool (&ok)[VPT],
                                          const RowArgs& a, float4* yrow, int64_t col4_base,
                                          int stride, int lane, const R& red, bool store = true) {
@@ -179,7 +213,7 @@ __device__ __forceinline__ void row_math(float4 (&v)[VPT], const bool (&ok)[VPT]
 #pragma unroll
     for (int k = 0; k < VPT; ++k)
       if (ok[k] && store) {
-        const int64_t c4 = col4_base + (int64_t)k * stride + lane;
+        const int64_t c4 = col4_base + vec_slot<PAIRED>(k, lane, stride);
         float4 r;
         r.x = (v[k].x - mean) * rstd;
         r.y = (v[k].y - mean) * rstd;
@@ -193,7 +227,7 @@ __device__ __forceinline__ void row_math(float4 (&v)[VPT], const bool (&ok)[VPT]
           const float4 b = __ldg(b4 + c4);
           r.x += b.x; r.y += b.y; r.z += b.z; r.w += b.w;
         }
-        st_stream(yrow + (int64_t)k * stride + lane, r);
+        v[k] = r;
       }
   } else if constexpr (OP == kRmsNorm) {
     float q = 0.0f;
@@ -206,7 +240,7 @@ __device__ __forceinline__ void row_math(float4 (&v)[VPT], const bool (&ok)[VPT]
 #pragma unroll
     for (int k = 0; k < VPT; ++k)
       if (ok[k] && store) {
-        const int64_t c4 = col4_base + (int64_t)k * stride + lane;
+        const int64_t c4 = col4_base + vec_slot<PAIRED>(k, lane, stride);
         float4 r;
         r.x = v[k].x * inv;
         r.y = v[k].y * inv;
@@ -216,7 +250,7 @@ __device__ __forceinline__ void row_math(float4 (&v)[VPT], const bool (&ok)[VPT]
           const float4 g = __ldg(g4 + c4);
           r.x *= g.x; r.y *= g.y; r.z *= g.z; r.w *= g.w;
         }
-        st_stream(yrow + (int64_t)k * stride + lane, r);
+        v[k] = r;
       }
   } else {
     // one pass: this thread's max and sum of exp(x - max), then a single
@@ -243,10 +277,7 @@ __device__ __forceinline__ void row_math(float4 (&v)[VPT], const bool (&ok)[VPT]
       const float scale = ms_rescale(mt, tot.m) / tot.s;
 #pragma unroll
       for (int k = 0; k < VPT; ++k)
-        if (ok[k] && store) {
-          float4 r = make_float4(v[k].x * scale, v[k].y * scale, v[k].z * scale, v[k].w * scale);
-          st_stream(yrow + (int64_t)k * stride + lane, r);
-        }
+        v[k] = make_float4(v[k].x * scale, v[k].y * scale, v[k].z * scale, v[k].w * scale);
     } else {
 #pragma unroll
       for (int k = 0; k < VPT; ++k)
@@ -257,13 +288,10 @@ __device__ __forceinline__ void row_math(float4 (&v)[VPT], const bool (&ok)[VPT]
       const float m = tot.m, lse = logf(tot.s);
 #pragma unroll
       for (int k = 0; k < VPT; ++k)
-        if (ok[k] && store) {
-          float4 r = make_float4((v[k].x - m) - lse, (v[k].y - m) - lse, (v[k].z - m) - lse,
-                                 (v[k].w - m) - lse);
-          st_stream(yrow + (int64_t)k * stride + lane, r);
-        }
+        v[k] = make_float4((v[k].x - m) - lse, (v[k].y - m) - lse, (v[k].z - m) - lse, (v[k].w - m) - lse);
     }
   }
+  if (store) store_row<VPT, PAIRED>(yrow, v, ok, lane, stride);
 }
 
 // One CTA (or one CL-CTA cluster) per row; NT threads x VPT float4 each.
@@ -345,7 +373,7 @@ __device__ __forceinline__ void bulk_load(uint32_t dst, const void* src, uint32_
       : "memory");
 }
 
-template <RowOp OP, int NT, int VPT, int CL, int DEPTH>
+template <RowOp OP, int NT, int VPT, int CL, int DEPTH, bool PAIRED>
 __global__ void __launch_bounds__(NT) row_persist_kernel(RowArgs a) {
   extern __shared__ float4 seg_buf[];  // DEPTH segment buffers
   __shared__ float red[64];
@@ -385,7 +413,7 @@ __global__ void __launch_bounds__(NT) row_persist_kernel(RowArgs a) {
     bool ok[VPT];
 #pragma unroll
     for (int k = 0; k < VPT; ++k) {
-      const int j = k * NT + threadIdx.x;
+      const int64_t j = vec_slot<PAIRED>(k, threadIdx.x, NT);
       ok[k] = j < seg4;
       v[k] = (ok[k] && alive && got) ? buf[j] : make_float4(0.f, 0.f, 0.f, 0.f);
     }
@@ -399,15 +427,15 @@ __global__ void __launch_bounds__(NT) row_persist_kernel(RowArgs a) {
     if (threadIdx.x == 0 && alive && next < a.rows)
       bulk_load(smem_addr(buf), xseg + next * (int64_t)a.cols, seg_bytes, smem_addr(&bars[slot]));
     float4* ys = reinterpret_cast<float4*>(a.y + row * (int64_t)a.cols) + col4_base;
-    row_math<OP, VPT>(v, ok, a, ys, col4_base, NT, threadIdx.x, r, alive);
+    row_math<OP, VPT, PAIRED>(v, ok, a, ys, col4_base, NT, threadIdx.x, r, alive);
   }
   if constexpr (CL > 1)
     asm volatile("barrier.cluster.arrive.relaxed.aligned;\n\tbarrier.cluster.wait.aligned;" ::: "memory");
 }
 
-template <RowOp OP, int NT, int VPT, int CL, int DEPTH>
-cudaError_t launch_persist(const RowArgs& a, cudaStream_t s) {
-  auto kern = row_persist_kernel<OP, NT, VPT, CL, DEPTH>;
+template <RowOp OP, int NT, int VPT, int CL, int DEPTH, bool PAIRED>
+cudaError_t launch_persist_impl(const RowArgs& a, cudaStream_t s) {
+  auto kern = row_persist_kernel<OP, NT, VPT, CL, DEPTH, PAIRED>;
   const int smem = a.cols / CL * 4 * DEPTH;
   static uint64_t attr_set = 0;
   int dev = 0;
@@ -436,6 +464,14 @@ cudaError_t launch_persist(const RowArgs& a, cudaStream_t s) {
   nclusters = (int)std::max<int64_t>(1, std::min<int64_t>(nclusters, a.rows));
   cfg.gridDim = dim3((unsigned)(nclusters * CL));
   return cudaLaunchKernelEx(&cfg, kern, a);
+}
+
+// 256-bit result stores when every row segment starts on 32 bytes
+template <RowOp OP, int NT, int VPT, int CL, int DEPTH>
+cudaError_t launch_persist(const RowArgs& a, cudaStream_t s) {
+  if (aligned32(a.x) && aligned32(a.y) && a.cols % (8 * CL) == 0)
+    return launch_persist_impl<OP, NT, VPT, CL, DEPTH, true>(a, s);
+  return launch_persist_impl<OP, NT, VPT, CL, DEPTH, false>(a, s);
 }
 
 // One warp per row (rows of at most 32 * VPT * 4 floats); 4 warps per CTA.
