@@ -21,6 +21,14 @@ oracle's small shapes with CPU-seeded inputs exactly as the reference does.
 
     python tests/eval_b200.py --problem 40_LayerNorm --out v.json [--small]
     python tests/eval_b200.py --all --out-dir verdicts/ [--small]   # one subprocess each
+    torchrun --nproc-per-node N tests/eval_b200.py --problem P --out v.json   # N GPUs
+
+Under torchrun every rank runs the whole protocol on its own GPU at the same
+time (weak scaling: each GPU evaluates the full problem, L2 thrashed on every
+device): parity must hold on every rank, each timed arm starts after a
+barrier, and the verdict (written by rank 0) reports the max over ranks of
+the median times, the per-rank medians, `ngpu`, and GB/s or TFLOP/s of the
+whole job.
 """
 from __future__ import annotations
 
@@ -184,10 +192,45 @@ def _cpu_time(name: str, target_s: float = 0.2, max_bytes: int = 512 << 20) -> d
         rows *= 4
 
 
+def _ranks() -> tuple[int, int, int]:
+    """(rank, world, local rank) of a torchrun launch; (0, 1, 0) otherwise."""
+    return (int(os.environ.get("RANK", "0")), int(os.environ.get("WORLD_SIZE", "1")),
+            int(os.environ.get("LOCAL_RANK", "0")))
+
+
+def _all_ranks_ok(ok: bool, device) -> bool:
+    import torch.distributed as tdist
+
+    if not tdist.is_initialized():
+        return ok
+    t = torch.tensor([1 if ok else 0], dtype=torch.int32, device=device)
+    tdist.all_reduce(t, op=tdist.ReduceOp.MIN)
+    return bool(t.item())
+
+
+def _timed_all_ranks(fn, args, device, l2, trials) -> dict:
+    """time_fn on every rank at once; max over ranks of the medians."""
+    import torch.distributed as tdist
+
+    if not tdist.is_initialized():
+        return time_fn(fn, args, device, l2, trials)
+    tdist.barrier(device_ids=[device.index])
+    r = time_fn(fn, args, device, l2, trials)
+    meds = [torch.zeros(1, dtype=torch.float64, device=device) for _ in range(tdist.get_world_size())]
+    tdist.all_gather(meds, torch.tensor([r["median_ms"]], dtype=torch.float64, device=device))
+    per_rank = [round(m.item(), 6) for m in meds]
+    r["per_rank_median_ms"] = per_rank
+    r["median_ms"] = max(per_rank)
+    return r
+
+
 def evaluate(name: str, out_path: str | None = None, small: bool = False, trials: int = TRIALS,
              with_compile: bool = False, with_cpu: bool = True) -> dict:
-    device = torch.device("cuda:0")
+    rank, world, local = _ranks()
+    device = torch.device("cuda", local)
     torch.cuda.set_device(device)
+    if rank != 0:
+        out_path = None  # rank 0 writes the verdict
     path = candidate_path(name)
     src = path.read_text()
     Model_ref, _, get_init_inputs, _ = problems.load_problem(name, "small" if small else None)
@@ -197,7 +240,8 @@ def evaluate(name: str, out_path: str | None = None, small: bool = False, trials
     v = {"problem": name, "candidate": str(path.relative_to(REPO)), "eval_sha": EVAL_SHA,
          "tol": REF_TOL, "op_tol": tol,
          "op_reference": "float64" if name in OP_REFERENCE_F64 else "float32 eager", "warmup": WARMUP, "trials": trials, "torch": torch.__version__,
-         "device": torch.cuda.get_device_name(device), "shapes": "small" if small else "benchmark"}
+         "device": torch.cuda.get_device_name(device), "shapes": "small" if small else "benchmark",
+         "ngpu": world}
     entry = candidate_entry(src)
     v["static_check"] = static_check(src, entry)
     if not v["static_check"]["ok"]:
@@ -246,20 +290,23 @@ def evaluate(name: str, out_path: str | None = None, small: bool = False, trials
         again = cand_model(*inputs0)
     r2 = 0 in digests and digest_close(digests[0], digest(again.float()))
     del again
-    v["parity"] = {"parity": passed == len(SEEDS) and r2, "trials_passed": passed, "recompute_check": r2,
+    ok_all = _all_ranks_ok(passed == len(SEEDS) and r2, device)
+    v["parity"] = {"parity": ok_all, "trials_passed": passed, "recompute_check": r2,
                    "trials": trials_out}
+    if world > 1:
+        v["parity"]["all_ranks"] = ok_all
     if not v["parity"]["parity"]:
         v.update(milestone=-1, why="parity failed")
         return _write(out_path, v)
 
     with torch.no_grad():
-        v["cand_time"] = time_fn(cand_model, inputs0, device, l2, trials)
-        v["eager_time"] = time_fn(ref_model, inputs0, device, l2, trials)
+        v["cand_time"] = _timed_all_ranks(cand_model, inputs0, device, l2, trials)
+        v["eager_time"] = _timed_all_ranks(ref_model, inputs0, device, l2, trials)
         if with_compile:
             try:
                 torch._dynamo.reset()
                 cm = torch.compile(ref_model, backend="inductor", mode="default")
-                v["compiled_time"] = time_fn(cm, inputs0, device, l2, trials)
+                v["compiled_time"] = _timed_all_ranks(cm, inputs0, device, l2, trials)
             except Exception as e:  # noqa: BLE001
                 v["compiled_time"] = None
                 v["compiled_error"] = repr(e)[:300]
@@ -275,17 +322,17 @@ def evaluate(name: str, out_path: str | None = None, small: bool = False, trials
     if not small:
         w = _workload(name)
         v["algo_bytes"] = w.algo_bytes
-        v["gbs"] = round(w.algo_bytes / (c * 1e-3) / 1e9, 1)
+        v["gbs"] = round(w.algo_bytes * world / (c * 1e-3) / 1e9, 1)  # whole job
         if w.flops:
-            v["tflops"] = round(w.flops / (c * 1e-3) / 1e12, 2)
+            v["tflops"] = round(w.flops * world / (c * 1e-3) / 1e12, 2)
         peaks = _peaks()
         if w.bound == "tensor":
-            v["roofline_frac"] = round(v["tflops"] / (TF32_BURST_TFLOPS / 3.0), 4)
-            v["roofline"] = "3xTF32 = measured TF32 burst / 3"
+            v["roofline_frac"] = round(v["tflops"] / world / (TF32_BURST_TFLOPS / 3.0), 4)
+            v["roofline"] = "3xTF32 = measured TF32 burst / 3 (per GPU)"
         else:
-            v["roofline_frac"] = round(v["gbs"] / peaks["hbm_gbs"], 4)
-            v["roofline"] = f"HBM copy {peaks['hbm_gbs']} GB/s ({peaks['source']})"
-        if with_cpu:
+            v["roofline_frac"] = round(v["gbs"] / world / peaks["hbm_gbs"], 4)
+            v["roofline"] = f"HBM copy {peaks['hbm_gbs']} GB/s per GPU ({peaks['source']})"
+        if with_cpu and rank == 0:
             try:
                 v["cpu"] = _cpu_time(name)
             except Exception as ex:  # noqa: BLE001
@@ -342,13 +389,32 @@ def main() -> int:
     ap.add_argument("--compile", action="store_true", help="also time torch.compile(inductor)")
     ap.add_argument("--no-cpu", action="store_true")
     a = ap.parse_args()
+    rank, world, local = _ranks()
     if a.all:
+        if world > 1:
+            ap.error("--all runs one subprocess per problem on one GPU; use --problem under torchrun")
         extra = ["--trials", str(a.trials)] + (["--compile"] if a.compile else []) + (
             ["--no-cpu"] if a.no_cpu else [])
         return run_all(a.out_dir, a.small, extra=extra)
-    v = evaluate(a.problem, a.out, a.small, a.trials, a.compile, not a.no_cpu)
-    print(json.dumps({k: v.get(k) for k in ("problem", "milestone", "speedup_eager", "gbs", "tflops",
-                                            "roofline_frac", "why")}, default=str))
+    if world > 1:
+        import datetime
+
+        import torch.distributed as tdist
+
+        torch.cuda.set_device(local)
+        tdist.init_process_group("nccl", device_id=torch.device("cuda", local),
+                                 timeout=datetime.timedelta(seconds=300))
+    try:
+        v = evaluate(a.problem, a.out, a.small, a.trials, a.compile, not a.no_cpu)
+    finally:
+        if world > 1:
+            import torch.distributed as tdist
+
+            tdist.barrier()
+            tdist.destroy_process_group()
+    if rank == 0:
+        print(json.dumps({k: v.get(k) for k in ("problem", "ngpu", "milestone", "speedup_eager", "gbs",
+                                                "tflops", "roofline_frac", "why")}, default=str))
     return 0
 
 

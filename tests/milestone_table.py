@@ -2,8 +2,9 @@
 
 The reference builds results/milestone-table.{md,json} from its verdicts
 (scripts/milestone_table.py:27-84); this version adds the B200 columns:
-GB/s or TFLOP/s, fraction of the measured roofline, and the torch-eager CPU
-estimate with its core count.
+the GPU count of the verdict, GB/s or TFLOP/s of the whole job, fraction of
+the measured per-GPU roofline, and the torch-eager CPU estimate with its core
+count.
 
     python tests/milestone_table.py verdicts/ [--md out.md] [--json out.json]
 """
@@ -24,7 +25,7 @@ def rows(verdicts: list[dict]) -> list[dict]:
     for v in verdicts:
         ct, et = v.get("cand_time") or {}, v.get("eager_time") or {}
         cpu = v.get("cpu") or {}
-        r = {"problem": v.get("problem"), "milestone": v.get("milestone"),
+        r = {"problem": v.get("problem"), "ngpu": v.get("ngpu", 1), "milestone": v.get("milestone"),
              "cand_ms": ct.get("median_ms"), "eager_ms": et.get("median_ms"),
              "speedup_eager": v.get("speedup_eager"), "gbs": v.get("gbs"), "tflops": v.get("tflops"),
              "roofline_frac": v.get("roofline_frac"), "cpu_ms": cpu.get("full_ms_estimate"),
@@ -36,11 +37,12 @@ def rows(verdicts: list[dict]) -> list[dict]:
 
 
 def markdown(rs: list[dict]) -> str:
-    head = ("| problem | milestone | cand ms | eager ms | x eager | GB/s | TFLOP/s | roofline | "
-            "CPU ms (est.) | x CPU |\n|---|---:|---:|---:|---:|---:|---:|---:|---:|---:|\n")
+    head = ("| problem | ngpu | milestone | cand ms | eager ms | x eager | GB/s | TFLOP/s | roofline | "
+            "CPU ms (est.) | x CPU |\n|---|---:|---:|---:|---:|---:|---:|---:|---:|---:|---:|\n")
     fmt = lambda x: "" if x is None else str(x)  # noqa: E731
     body = "".join(
-        f"| {r['problem']} | {fmt(r['milestone'])} | {fmt(r['cand_ms'])} | {fmt(r['eager_ms'])} | "
+        f"| {r['problem']} | {fmt(r['ngpu'])} | {fmt(r['milestone'])} | {fmt(r['cand_ms'])} | "
+        f"{fmt(r['eager_ms'])} | "
         f"{fmt(r['speedup_eager'])} | {fmt(r['gbs'])} | {fmt(r['tflops'])} | {fmt(r['roofline_frac'])} | "
         f"{fmt(r['cpu_ms'])} | {fmt(r.get('x_cpu'))} |\n" for r in rs)
     return head + body

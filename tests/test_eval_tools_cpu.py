@@ -11,12 +11,13 @@ def test_table_from_verdicts(tmp_path):
     (tmp_path / "a.json").write_text(json.dumps({
         "problem": "40_LayerNorm", "milestone": 2, "cand_time": {"median_ms": 0.63},
         "eager_time": {"median_ms": 1.9}, "speedup_eager": 3.0, "gbs": 6800.0,
-        "roofline_frac": 1.04, "cpu": {"full_ms_estimate": 210.0, "cores": 16}}))
+        "roofline_frac": 1.04, "cpu": {"full_ms_estimate": 210.0, "cores": 16}, "ngpu": 2}))
     (tmp_path / "b.json").write_text(json.dumps({"problem": "x", "milestone": -1, "why": "parity failed"}))
     rs = rows(load(str(tmp_path)))
     assert rs[0]["x_cpu"] == round(210.0 / 0.63, 1)
     md = markdown(rs)
-    assert "| 40_LayerNorm | 2 |" in md and "| x | -1 |" in md
+    # ngpu column: from the verdict, 1 for a single-GPU verdict without it
+    assert "| 40_LayerNorm | 2 | 2 |" in md and "| x | 1 | -1 |" in md
 
 
 def test_word_fingerprint_sees_single_changes_and_swaps():

@@ -137,3 +137,25 @@ def test_sharded_ops_on_two_gpus():
         assert status == "ok", res
         for name, (got, want, tol) in res.items():
             np.testing.assert_allclose(got, want, rtol=tol, atol=tol, err_msg=f"rank {rank} {name}")
+
+
+def test_strict_eval_on_two_gpus(tmp_path):
+    """The strict eval sibling under torchrun: every rank checks parity and
+    times the candidate on its own GPU; rank 0's verdict carries ngpu 2, the
+    per-rank medians and their max."""
+    if torch.cuda.device_count() < 2:
+        pytest.skip("needs 2 GPUs")
+    import json
+    import subprocess
+
+    out = tmp_path / "v.json"
+    env = dict(os.environ, NCCL_NVLS_ENABLE="0")
+    cmd = [sys.executable, "-m", "torch.distributed.run", "--nnodes=1", "--nproc-per-node", "2",
+           "--master-addr", "127.0.0.1", "--master-port", str(_free_port()), str(REPO / "tests" / "eval_b200.py"),
+           "--problem", "40_LayerNorm", "--small", "--trials", "5", "--no-cpu", "--out", str(out)]
+    r = subprocess.run(cmd, env=env, capture_output=True, text=True, timeout=600)
+    assert r.returncode == 0, r.stderr[-2000:]
+    v = json.loads(out.read_text())
+    assert v["ngpu"] == 2 and v["parity"]["parity"] and v["parity"]["all_ranks"]
+    per = v["cand_time"]["per_rank_median_ms"]
+    assert len(per) == 2 and v["cand_time"]["median_ms"] == max(per)
