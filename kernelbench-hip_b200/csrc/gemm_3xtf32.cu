@@ -48,6 +48,23 @@
 // shared abort flag and a device fault word, all roles leave their loops,
 // outstanding TMA loads are drained (bounded) and TMEM is freed.
 //
+// Small K (at most kResKB 16-deep K blocks, e.g. [32768, 64] x [64, 32768]):
+// a tile is only a few K blocks deep, so reloading and re-splitting the B
+// tile for every output tile dominates.  The B-resident form (RES) keeps one
+// tile column's whole B panel, raw and lo, in shared memory (128 KB) and
+// streams only A through the ring.  Every tile column is cut into runs of
+// p.run m-tiles; run r (segment-major: all columns' first segments, then
+// the second ones, ...) goes to CTA r mod gridDim.x, which walks its runs in
+// order.  So a CTA stays on one panel for a whole run, and the CTAs working
+// at the same time hold horizontally adjacent tiles of one row band, as in
+// the streaming form (an order that scattered concurrent tiles over C wrote
+// 5-10 % slower).  At each run start the producer waits until the MMAs of
+// the previous run are done (panel_empty, a tcgen05.commit), loads the new
+// panel, the converters split it (panel_full -> panel_conv) and the MMA warp
+// waits for panel_conv.  A run in a column's last segment ends at the last
+// m-tile.  MMA order, chunking and the epilogue are those of the streaming
+// form, so results are bitwise identical.
+//
 // Shapes the TMA path cannot describe (row strides not multiples of 16 bytes,
 // unaligned bases) take a CUDA-core fp32 kernel.
 #include <cuda.h>
@@ -75,18 +92,24 @@ constexpr uint64_t kWaitLimitNs = 2000000000ull;
 constexpr int kBoxRows = 32, kBoxCols = 32;      // C store box: 32 rows x 128 B
 constexpr int kBoxBytes = kBoxRows * kBoxCols * 4;
 
-template <int BN>
+constexpr int kResKB = 4;  // B-resident form: K blocks the shared-memory B panel holds
+
+template <int BN, bool RES = false>
 struct Cfg {
   static constexpr int A_BYTES = BM * BK * 4;                  // 8 KB
   static constexpr int B_BYTES = BN * BK * 4;                  // 16 KB (BN 256)
-  static constexpr int STAGE_BYTES = 2 * (A_BYTES + B_BYTES);  // raw + lo buffers
+  // ring stage: raw + lo of A and B (streaming form) or of A only (B resident)
+  static constexpr int STAGE_BYTES = RES ? 2 * A_BYTES : 2 * (A_BYTES + B_BYTES);
+  static constexpr int PANEL_BYTES = RES ? kResKB * 2 * B_BYTES : 0;  // [kb][raw | lo]
   static constexpr int STAGING_BYTES = kPromoWarps * kBoxBytes;  // one C box per promotion warp
   static constexpr int BAR_BYTES = 256;
   static constexpr int SMEM_BYTES =
-      kStages * STAGE_BYTES + STAGING_BYTES + BAR_BYTES + 1024;  // + alignment slack
+      kStages * STAGE_BYTES + PANEL_BYTES + STAGING_BYTES + BAR_BYTES + 1024;  // + alignment slack
   static constexpr int TMEM_COLS = 2 * BN;                     // two chunk accumulators
   static constexpr int COLS_PER_WARP = BN / 2;                 // promotion warps split columns
 };
+static_assert(Cfg<256, true>::SMEM_BYTES <= 232448, "B-resident form exceeds shared memory");
+static_assert(Cfg<256, false>::SMEM_BYTES <= 232448, "streaming form exceeds shared memory");
 
 // ------------------------------------------------------------------ PTX wrappers
 __device__ __forceinline__ uint32_t smem_u32(const void* p) {
@@ -274,19 +297,65 @@ struct Params {
   int kb_per_split;  // mode 1: k-blocks per split
   int mode;          // 0: z = batch index, 1: z = split index (write partials)
   int tma_store;     // 1: epilogue through shared memory + TMA tensor stores (tmC)
-  int tiles_n, tiles_m, tiles_z;  // output tile grid, n fastest
+  int tiles_n, tiles_m, tiles_z;  // output tile grid
+  int run, runs;     // B-resident form: m-tiles per run, runs in all (tiles_z x tiles_n x segments);
+                     // streaming form (run 0): tiles blockIdx.x + i * gridDim.x, n fastest
+  int segs;          // B-resident form: runs per tile column
 };
 
 // One output tile: its corner, batch / split index and k-block range.
 struct Tile {
   int n0, m0, z, batch, kb_begin, nk;
 };
-__device__ __forceinline__ Tile tile_at(const Params& p, int t, int bn, int nk_total) {
+// A run: tiles (z, n0, m-tiles mt0 .. mt0 + len - 1).  B-resident form: run
+// r of all p.runs, segment-major; streaming form: tile id r (n fastest), len 1.
+struct Run {
+  int z, n0, mt0, len;
+};
+template <bool RES>
+__device__ __forceinline__ Run run_at(const Params& p, int r, int bn) {
+  Run R;
+  if (RES) {
+    const int per_z = p.tiles_n * p.segs;
+    R.z = r / per_z;
+    const int rest = r - R.z * per_z;
+    const int seg = rest / p.tiles_n;
+    R.n0 = (rest - seg * p.tiles_n) * bn;
+    R.mt0 = seg * p.run;
+    R.len = min(p.run, p.tiles_m - R.mt0);
+  } else {
+    const int rest = r / p.tiles_n;
+    R.n0 = (r - rest * p.tiles_n) * bn;
+    R.mt0 = rest % p.tiles_m;
+    R.z = rest / p.tiles_m;
+    R.len = 1;
+  }
+  return R;
+}
+template <bool RES>
+__device__ __forceinline__ int run_count(const Params& p, int ntiles) {
+  return RES ? p.runs : ntiles;
+}
+// The run's length, and its jt-th tile; both recompute the run from r, so
+// that only r and jt stay live in the loops (the promotion warps hold 128
+// accumulators each).
+template <bool RES>
+__device__ __forceinline__ int run_len(const Params& p, int r, int bn) {
+  return RES ? run_at<RES>(p, r, bn).len : 1;
+}
+// Step (r, jt) to this CTA's next tile.
+template <bool RES>
+__device__ __forceinline__ void next_in_walk(const Params& p, int& r, int& jt, int bn) {
+  if (++jt >= run_len<RES>(p, r, bn)) {
+    jt = 0;
+    r += (int)gridDim.x;
+  }
+}
+__device__ __forceinline__ Tile tile_in(const Params& p, const Run& R, int j, int nk_total) {
   Tile T;
-  const int rest = t / p.tiles_n;
-  T.n0 = (t - rest * p.tiles_n) * bn;
-  T.m0 = (rest % p.tiles_m) * BM;
-  T.z = rest / p.tiles_m;
+  T.n0 = R.n0;
+  T.m0 = (R.mt0 + j) * BM;
+  T.z = R.z;
   T.batch = T.z;
   T.kb_begin = 0;
   int kb_end = nk_total;
@@ -299,18 +368,20 @@ __device__ __forceinline__ Tile tile_at(const Params& p, int t, int bn, int nk_t
   return T;
 }
 
-template <int BN, bool TRANS_A>
+template <int BN, bool TRANS_A, bool RES>
 __global__ void __launch_bounds__(kThreads, 1)
 gemm3x_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUtensorMap tmB,
               const __grid_constant__ CUtensorMap tmC, Params p) {
-  using CF = Cfg<BN>;
+  using CF = Cfg<BN, RES>;
   constexpr int S = kStages;
   extern __shared__ uint8_t smem_raw[];
   uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
-  uint8_t* staging = smem + S * CF::STAGE_BYTES;  // 1024-aligned: STAGE_BYTES is a multiple of 1 KB
+  uint8_t* panel = smem + S * CF::STAGE_BYTES;    // B panel (B-resident form), 1024-aligned
+  uint8_t* staging = panel + CF::PANEL_BYTES;     // 1024-aligned: all sizes above are multiples of 1 KB
   uint64_t* bars = reinterpret_cast<uint64_t*>(staging + CF::STAGING_BYTES);
-  // bars: [0,S) full, [S,2S) conv, [2S,3S) empty, [3S,3S+2) chunk_full, [3S+2,3S+4) chunk_empty
-  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(bars + 3 * S + 4);
+  // bars: [0,S) full, [S,2S) conv, [2S,3S) empty, [3S,3S+2) chunk_full, [3S+2,3S+4) chunk_empty,
+  //       3S+4 panel_full, 3S+5 panel_conv, 3S+6 panel_empty
+  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(bars + 3 * S + 7);
   volatile int* abort_flag = reinterpret_cast<volatile int*>(tmem_slot + 1);
 
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
@@ -322,6 +393,9 @@ gemm3x_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ C
   auto empty = [&](int s) { return smem_u32(bars + 2 * S + s); };
   auto chunk_full = [&](int b) { return smem_u32(bars + 3 * S + b); };
   auto chunk_empty = [&](int b) { return smem_u32(bars + 3 * S + 2 + b); };
+  const uint32_t panel_full = smem_u32(bars + 3 * S + 4);
+  const uint32_t panel_conv = smem_u32(bars + 3 * S + 5);
+  const uint32_t panel_empty = smem_u32(bars + 3 * S + 6);
 
   if (threadIdx.x == 0) {
     for (int s = 0; s < S; ++s) {
@@ -333,6 +407,9 @@ gemm3x_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ C
       mbar_init(chunk_full(b), 1);
       mbar_init(chunk_empty(b), kPromoThreads);
     }
+    mbar_init(panel_full, 1);
+    mbar_init(panel_conv, kConvThreads);
+    mbar_init(panel_empty, 1);
     *abort_flag = 0;
     fence_barrier_init();
   }
@@ -354,30 +431,46 @@ gemm3x_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ C
     if (warp == 0) {
       // ---------------- TMA producer
       if (lane == 0) {
-        int g = 0;
+        int g = 0, np = 0;
         bool alive = true;
-        for (int t = blockIdx.x; t < ntiles && alive; t += gridDim.x) {
-          const Tile T = tile_at(p, t, BN, nk_total);
-          for (int it = 0; it < T.nk; ++it) {
-            const int s = g % S;
-            if (!mbar_wait(empty(s), ((g / S) & 1) ^ 1, abort_flag)) {
-              alive = false;
-              break;
-            }
-            uint8_t* st = stage_ptr(s);
-            const int k0 = (T.kb_begin + it) * BK;
-            mbar_expect_tx(full(s), CF::A_BYTES + CF::B_BYTES);
-            if (TRANS_A) {
+        for (int r = blockIdx.x; r < run_count<RES>(p, ntiles) && alive; r += gridDim.x) {
+          if (RES) {
+            const Run R = run_at<RES>(p, r, BN);
+            // the previous panel's MMAs must be done before it is overwritten
+            if (!mbar_wait(panel_empty, (np & 1) ^ 1, abort_flag)) break;
+            mbar_expect_tx(panel_full, nk_total * CF::B_BYTES);
+            for (int kb = 0; kb < nk_total; ++kb)
 #pragma unroll
-              for (int j = 0; j < BM / 32; ++j)
-                tma_load_3d(smem_u32(st + j * 2048), &tmA, full(s), T.m0 + 32 * j, k0, T.batch);
-            } else {
-              tma_load_3d(smem_u32(st), &tmA, full(s), k0, T.m0, T.batch);
-            }
+              for (int j = 0; j < BN / 32; ++j)
+                tma_load_3d(smem_u32(panel + kb * 2 * CF::B_BYTES + j * 2048), &tmB, panel_full, R.n0 + 32 * j,
+                            kb * BK, R.z);
+            ++np;
+          }
+          for (int jt = 0; jt < run_len<RES>(p, r, BN) && alive; ++jt) {
+            const Tile T = tile_in(p, run_at<RES>(p, r, BN), jt, nk_total);
+            for (int it = 0; it < T.nk; ++it) {
+              const int s = g % S;
+              if (!mbar_wait(empty(s), ((g / S) & 1) ^ 1, abort_flag)) {
+                alive = false;
+                break;
+              }
+              uint8_t* st = stage_ptr(s);
+              const int k0 = (T.kb_begin + it) * BK;
+              mbar_expect_tx(full(s), RES ? CF::A_BYTES : CF::A_BYTES + CF::B_BYTES);
+              if (TRANS_A) {
 #pragma unroll
-            for (int j = 0; j < BN / 32; ++j)
-              tma_load_3d(smem_u32(st + CF::A_BYTES + j * 2048), &tmB, full(s), T.n0 + 32 * j, k0, T.batch);
-            ++g;
+                for (int j = 0; j < BM / 32; ++j)
+                  tma_load_3d(smem_u32(st + j * 2048), &tmA, full(s), T.m0 + 32 * j, k0, T.batch);
+              } else {
+                tma_load_3d(smem_u32(st), &tmA, full(s), k0, T.m0, T.batch);
+              }
+              if (!RES) {
+#pragma unroll
+                for (int j = 0; j < BN / 32; ++j)
+                  tma_load_3d(smem_u32(st + CF::A_BYTES + j * 2048), &tmB, full(s), T.n0 + 32 * j, k0, T.batch);
+              }
+              ++g;
+            }
           }
         }
         // drain: every issued load must land before the CTA may exit
@@ -388,75 +481,113 @@ gemm3x_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ C
             if (globaltimer() - t0 > kWaitLimitNs) break;
           }
         }
+        if (np > 0) {
+          const uint64_t t0 = globaltimer();
+          while (!mbar_try_wait(panel_full, (np - 1) & 1)) {
+            if (globaltimer() - t0 > kWaitLimitNs) break;
+          }
+        }
       }
     } else if (warp == 1) {
       // ---------------- MMA issuer
       if (lane == 0) {
         constexpr uint32_t idesc = make_idesc(BM, BN, TRANS_A);
-        int g = 0, gc = 0;
+        int g = 0, gc = 0, np = 0;
         bool alive = true;
-        for (int t = blockIdx.x; t < ntiles && alive; t += gridDim.x) {
-          const Tile T = tile_at(p, t, BN, nk_total);
-          for (int it = 0; it < T.nk; ++it, ++g) {
-            const int s = g % S;
-            const int b = gc & 1;
-            const bool chunk_first = (it % kChunkBlocks) == 0;
-            const bool chunk_last = (it % kChunkBlocks) == kChunkBlocks - 1 || it == T.nk - 1;
-            if (chunk_first && !mbar_wait(chunk_empty(b), ((gc >> 1) & 1) ^ 1, abort_flag)) {
-              alive = false;
-              break;
-            }
-            if (!mbar_wait(conv(s), (g / S) & 1, abort_flag)) {
-              alive = false;
-              break;
-            }
-            tc_fence_after();
-            uint8_t* st = stage_ptr(s);
-            const uint32_t a_hi = smem_u32(st);
-            const uint32_t b_hi = a_hi + CF::A_BYTES;
-            const uint32_t a_lo = b_hi + CF::B_BYTES;
-            const uint32_t b_lo = a_lo + CF::A_BYTES;
-            const uint32_t d = tmem + (uint32_t)(b * BN);
+        for (int r = blockIdx.x; r < run_count<RES>(p, ntiles) && alive; r += gridDim.x) {
+          if (RES) {
+            if (!mbar_wait(panel_conv, np & 1, abort_flag)) break;
+            ++np;
+          }
+          for (int jt = 0; jt < run_len<RES>(p, r, BN) && alive; ++jt) {
+            const Tile T = tile_in(p, run_at<RES>(p, r, BN), jt, nk_total);
+            for (int it = 0; it < T.nk; ++it, ++g) {
+              const int s = g % S;
+              const int b = gc & 1;
+              const bool chunk_first = (it % kChunkBlocks) == 0;
+              const bool chunk_last = (it % kChunkBlocks) == kChunkBlocks - 1 || it == T.nk - 1;
+              if (chunk_first && !mbar_wait(chunk_empty(b), ((gc >> 1) & 1) ^ 1, abort_flag)) {
+                alive = false;
+                break;
+              }
+              if (!mbar_wait(conv(s), (g / S) & 1, abort_flag)) {
+                alive = false;
+                break;
+              }
+              tc_fence_after();
+              uint8_t* st = stage_ptr(s);
+              uint32_t a_hi, a_lo, b_hi, b_lo;
+              if (RES) {
+                a_hi = smem_u32(st);
+                a_lo = a_hi + CF::A_BYTES;
+                b_hi = smem_u32(panel + it * 2 * CF::B_BYTES);
+                b_lo = b_hi + CF::B_BYTES;
+              } else {
+                a_hi = smem_u32(st);
+                b_hi = a_hi + CF::A_BYTES;
+                a_lo = b_hi + CF::B_BYTES;
+                b_lo = a_lo + CF::A_BYTES;
+              }
+              const uint32_t d = tmem + (uint32_t)(b * BN);
 #pragma unroll
-            for (int kk = 0; kk < BK / 8; ++kk) {
-              const uint32_t aoff = TRANS_A ? kk * 1024 : kk * 32;
-              const uint32_t boff = kk * 1024;
-              const uint64_t dah = TRANS_A ? desc_mnmajor(a_hi + aoff) : desc_kmajor(a_hi + aoff);
-              const uint64_t dal = TRANS_A ? desc_mnmajor(a_lo + aoff) : desc_kmajor(a_lo + aoff);
-              const uint64_t dbh = desc_mnmajor(b_hi + boff);
-              const uint64_t dbl = desc_mnmajor(b_lo + boff);
-              mma_tf32(d, dal, dbh, idesc, (chunk_first && kk == 0) ? 0u : 1u);
-              mma_tf32(d, dah, dbl, idesc, 1u);
-              mma_tf32(d, dah, dbh, idesc, 1u);
-            }
-            mma_commit(empty(s));
-            if (chunk_last) {
-              mma_commit(chunk_full(b));
-              ++gc;
+              for (int kk = 0; kk < BK / 8; ++kk) {
+                const uint32_t aoff = TRANS_A ? kk * 1024 : kk * 32;
+                const uint32_t boff = kk * 1024;
+                const uint64_t dah = TRANS_A ? desc_mnmajor(a_hi + aoff) : desc_kmajor(a_hi + aoff);
+                const uint64_t dal = TRANS_A ? desc_mnmajor(a_lo + aoff) : desc_kmajor(a_lo + aoff);
+                const uint64_t dbh = desc_mnmajor(b_hi + boff);
+                const uint64_t dbl = desc_mnmajor(b_lo + boff);
+                mma_tf32(d, dal, dbh, idesc, (chunk_first && kk == 0) ? 0u : 1u);
+                mma_tf32(d, dah, dbl, idesc, 1u);
+                mma_tf32(d, dah, dbh, idesc, 1u);
+              }
+              mma_commit(empty(s));
+              if (chunk_last) {
+                mma_commit(chunk_full(b));
+                ++gc;
+              }
             }
           }
+          // end of a run: release the panel once its MMAs complete
+          if (RES && alive) mma_commit(panel_empty);
         }
       }
     } else {
       // ---------------- lo converters (warps 2..7)
       const int t0 = threadIdx.x - kConvWarp0 * 32;
-      int g = 0;
+      int g = 0, np = 0;
       bool alive = true;
-      for (int t = blockIdx.x; t < ntiles && alive; t += gridDim.x) {
-        const Tile T = tile_at(p, t, BN, nk_total);
-        for (int it = 0; it < T.nk; ++it, ++g) {
-          const int s = g % S;
-          if (!mbar_wait(full(s), (g / S) & 1, abort_flag)) {
-            alive = false;
-            break;
-          }
-          uint8_t* st = stage_ptr(s);
-          lo_buffer(reinterpret_cast<const float4*>(st),
-                    reinterpret_cast<float4*>(st + CF::A_BYTES + CF::B_BYTES), CF::A_BYTES / 16, t0);
-          lo_buffer(reinterpret_cast<const float4*>(st + CF::A_BYTES),
-                    reinterpret_cast<float4*>(st + 2 * CF::A_BYTES + CF::B_BYTES), CF::B_BYTES / 16, t0);
+      for (int r = blockIdx.x; r < run_count<RES>(p, ntiles) && alive; r += gridDim.x) {
+        if (RES) {
+          if (!mbar_wait(panel_full, np & 1, abort_flag)) break;
+          for (int kb = 0; kb < nk_total; ++kb)
+            lo_buffer(reinterpret_cast<const float4*>(panel + kb * 2 * CF::B_BYTES),
+                      reinterpret_cast<float4*>(panel + kb * 2 * CF::B_BYTES + CF::B_BYTES), CF::B_BYTES / 16, t0);
           fence_proxy_async();
-          mbar_arrive(conv(s));
+          mbar_arrive(panel_conv);
+          ++np;
+        }
+        for (int jt = 0; jt < run_len<RES>(p, r, BN) && alive; ++jt) {
+          const Tile T = tile_in(p, run_at<RES>(p, r, BN), jt, nk_total);
+          for (int it = 0; it < T.nk; ++it, ++g) {
+            const int s = g % S;
+            if (!mbar_wait(full(s), (g / S) & 1, abort_flag)) {
+              alive = false;
+              break;
+            }
+            uint8_t* st = stage_ptr(s);
+            if (RES) {
+              lo_buffer(reinterpret_cast<const float4*>(st), reinterpret_cast<float4*>(st + CF::A_BYTES),
+                        CF::A_BYTES / 16, t0);
+            } else {
+              lo_buffer(reinterpret_cast<const float4*>(st),
+                        reinterpret_cast<float4*>(st + CF::A_BYTES + CF::B_BYTES), CF::A_BYTES / 16, t0);
+              lo_buffer(reinterpret_cast<const float4*>(st + CF::A_BYTES),
+                        reinterpret_cast<float4*>(st + 2 * CF::A_BYTES + CF::B_BYTES), CF::B_BYTES / 16, t0);
+            }
+            fence_proxy_async();
+            mbar_arrive(conv(s));
+          }
         }
       }
     }
@@ -470,8 +601,10 @@ gemm3x_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ C
     uint8_t* box = staging + pw * kBoxBytes;        // this warp's 32 x 32 C box
     int gc = 0;
     bool ok = true;
-    for (int t = blockIdx.x; t < ntiles && ok; t += gridDim.x) {
-      const Tile T = tile_at(p, t, BN, nk_total);
+    // one flat loop over this CTA's tiles (run r, position jt): nested loops
+    // here cost the accumulators registers
+    for (int r = blockIdx.x, jt = 0; r < run_count<RES>(p, ntiles) && ok; next_in_walk<RES>(p, r, jt, BN)) {
+      const Tile T = tile_in(p, run_at<RES>(p, r, BN), jt, nk_total);
       const int nchunks = (T.nk + kChunkBlocks - 1) / kChunkBlocks;
       float tot[NCOL];
 #pragma unroll
@@ -641,19 +774,56 @@ int make_store_map(CUtensorMap* tm, float* base, int64_t N, int64_t M, int64_t Z
   return KB_OK;
 }
 
-template <int BN, bool TA>
+template <int BN, bool TA, bool RES = false>
 int launch_tc(const CUtensorMap& ta, const CUtensorMap& tb, const CUtensorMap& tc, const Params& p, dim3 grid,
               cudaStream_t s) {
-  auto kern = gemm3x_kernel<BN, TA>;
+  auto kern = gemm3x_kernel<BN, TA, RES>;
+  constexpr int smem = Cfg<BN, RES>::SMEM_BYTES;
   static uint64_t attr_set = 0;  // one bit per device ordinal
   int dev = 0;
   KB_CUDA(cudaGetDevice(&dev));
   if (dev < 64 && !(attr_set >> dev & 1)) {
-    KB_CUDA(cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, Cfg<BN>::SMEM_BYTES));
+    KB_CUDA(cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, smem));
     attr_set |= 1ull << dev;
   }
-  kern<<<grid, kThreads, Cfg<BN>::SMEM_BYTES, s>>>(ta, tb, tc, p);
+  kern<<<grid, kThreads, smem, s>>>(ta, tb, tc, p);
   return check_launch("gemm3x_kernel");
+}
+
+// B-resident form: pick the run length.  Cost of a choice, in tile times:
+// the runs the busiest CTA walks x (run length + kSwitchTiles for the panel
+// reload between runs).  Taken when it is within 20 % of the streaming form's
+// tiles per CTA: a B-resident tile is that much cheaper at 48-64 deep K
+// (measured on the B200 over 32768^2, 16384^2, 32768x8192, 8192x32768,
+// 65536x4096 and a 3x38400x1792 batch: 0.83-0.90 of the streaming time at
+// K = 64, 0.92-0.99 at K = 48, bitwise-identical output).  At K <= 32 the
+// streaming form is already near the output-write bound and the gain
+// turned into losses of up to 15 %, so it keeps those.
+constexpr int kResMinKB = 3;
+constexpr int kSwitchTiles = 2;
+struct ResPlan {
+  int run = 0, segs = 0, runs = 0;
+};
+bool plan_runs(int64_t tm, int64_t tn, int64_t tz, int sms, ResPlan* out) {
+  const int64_t ntiles = tm * tn * tz;
+  if (ntiles < 2 * (int64_t)sms || ntiles > 0x7fffffff) return false;
+  int64_t best_cost = -1;
+  for (int64_t segs = 1; segs <= std::min<int64_t>(tm, 1024); ++segs) {
+    const int64_t run = ceil_div(tm, segs);
+    if (ceil_div(tm, run) != segs) continue;  // the same run length as a smaller segs
+    const int64_t runs = tz * tn * segs;
+    if (runs > 0x7fffffff) break;
+    const int64_t per_cta = ceil_div(runs, (int64_t)sms);
+    const int64_t cost = per_cta * (run + kSwitchTiles);
+    if (best_cost < 0 || cost < best_cost) {
+      best_cost = cost;
+      out->run = (int)run;
+      out->segs = (int)segs;
+      out->runs = (int)runs;
+    }
+  }
+  const int64_t stream_cost = ceil_div(ntiles, (int64_t)sms);
+  return best_cost > 0 && best_cost * 5 <= stream_cost * 6;
 }
 
 struct GemmArgs {
@@ -745,9 +915,18 @@ int run_gemm(const GemmArgs& g, int splits, float* ws, cudaStream_t s, bool redu
   // persistent: one CTA per SM (the shared memory and TMEM footprints allow no more)
   const int64_t ntiles = (int64_t)grid.x * grid.y * grid.z;
   KB_REQUIRE(ntiles <= 0x7fffffff, KB_ERR_UNSUPPORTED, "gemm: too many tiles");
-  const dim3 pgrid((unsigned)std::min<int64_t>(ntiles, sm_count()), 1, 1);
+  dim3 pgrid((unsigned)std::min<int64_t>(ntiles, sm_count()), 1, 1);
+  ResPlan rp;
+  const bool res = bn256 && !g.trans_a && p.mode == 0 && nk <= kResKB && nk >= kResMinKB &&
+                   plan_runs(p.tiles_m, p.tiles_n, p.tiles_z, sm_count(), &rp);
   int st;
-  if (bn256)
+  if (res) {
+    p.run = rp.run;
+    p.segs = rp.segs;
+    p.runs = rp.runs;
+    pgrid.x = (unsigned)std::min(rp.runs, sm_count());
+    st = launch_tc<256, false, true>(ta, tb, tc, p, pgrid, s);
+  } else if (bn256)
     st = g.trans_a ? launch_tc<256, true>(ta, tb, tc, p, pgrid, s) : launch_tc<256, false>(ta, tb, tc, p, pgrid, s);
   else
     st = g.trans_a ? launch_tc<128, true>(ta, tb, tc, p, pgrid, s) : launch_tc<128, false>(ta, tb, tc, p, pgrid, s);

@@ -346,6 +346,26 @@ def test_sgemm_shapes(mnk, cuda_device):
     assert read_fault() == 0
 
 
+# B-resident small-K form (K of 33-64 and thousands of output tiles): the
+# run planner sends each of these shapes to it (runs of m-tiles per tile
+# column; ragged last m-tile and n-tile; K tails of 40 and 56; several
+# batches, so runs cross batch boundaries).
+@pytest.mark.parametrize("shape", [(1, 6000, 12000, 40), (3, 12800, 1792, 48), (2, 20000, 2300, 56)])
+def test_gemm_b_resident_small_k(shape, cuda_device):
+    from kbb200 import ops as K
+    from kbb200._lib import read_fault
+
+    bt, M, N, Kd = shape
+    g = torch.Generator(device=cuda_device).manual_seed(M + N + Kd)
+    A = torch.randn(bt, M, Kd, device=cuda_device, generator=g)
+    B = torch.randn(bt, Kd, N, device=cuda_device, generator=g)
+    run = (lambda: K.matmul(A[0], B[0])) if bt == 1 else (lambda: K.bmm(A, B))
+    got = run()
+    _gemm_check(got, A[0] if bt == 1 else A, B[0] if bt == 1 else B, f"b-resident {shape}", batched=bt > 1)
+    assert torch.equal(got, run()), "must be deterministic"
+    assert read_fault() == 0
+
+
 @pytest.mark.parametrize("mnk", [(512, 384, 256), (130, 260, 68), (4096, 2048, 136)])
 def test_sgemm_transposed_a(mnk, cuda_device):
     from kbb200 import ops as K
