@@ -285,6 +285,9 @@ __device__ __forceinline__ void row_math(float4 (&v)[VPT], const bool (&ok)[VPT]
           st += (exp2f(fmaf(v[k].x, kLog2e, -mtl)) + exp2f(fmaf(v[k].y, kLog2e, -mtl))) +
                 (exp2f(fmaf(v[k].z, kLog2e, -mtl)) + exp2f(fmaf(v[k].w, kLog2e, -mtl)));
       const MaxSum tot = red.maxsum(MaxSum{mt, st}, 0);
+      // (x - max) - log sum, in this order: x - (max + log sum) is 2 % faster
+      // but rounds max + log sum at max's magnitude (|max| ~ 1e4 gave errors
+      // of 1.7e-4 where this order stays exact to an ulp of the result)
       const float m = tot.m, lse = logf(tot.s);
 #pragma unroll
       for (int k = 0; k < VPT; ++k)
