@@ -116,9 +116,10 @@ KB_API int kb_argmax_dim1_f32(const float* x, int64_t* out, int64_t B, int64_t I
 KB_API size_t kb_mse_workspace_size(int64_t n);
 KB_API int kb_mse_f32(const float* a, const float* b, float* out, int64_t n,
                void* workspace, size_t workspace_bytes, kbStream stream);
-/* sharded form: partial[0] = sum((a - b)^2) over this shard, in fp64, so a
- * collective can add shards before kb_mse_finalize_f32 divides by the total
- * element count.                                                          */
+/* sharded form: partial[0] = sum((a - b)^2) over this shard and
+ * partial[1] = n, both fp64 (16 bytes), so one collective adds the sums and
+ * the counts of all shards; kb_mse_finalize_f32 divides by total_n, or by
+ * total[1] when total_n is 0 (shards of any sizes, empty ones included).  */
 KB_API int kb_mse_partial_f64(const float* a, const float* b, double* partial,
                        int64_t n, void* workspace, size_t workspace_bytes,
                        kbStream stream);
@@ -180,9 +181,11 @@ KB_API int kb_batchnorm_train_f32_noalloc(const float* x, const float* gamma,
                                           float momentum, float* running_mean,
                                           float* running_var, kbStream stream);
 /* sharded form: stats[0:C] = per-channel sum, stats[C:2C] = per-channel sum
- * of squares over this shard (fp64); a collective adds them across shards,
- * then kb_batchnorm_apply_f32 normalises with `total_count` elements per
- * channel.                                                                */
+ * of squares, stats[2C] = elements per channel (N * HW) over this shard,
+ * 2C + 1 doubles; a collective adds them across shards, then
+ * kb_batchnorm_apply_f32 normalises with `total_count` elements per channel,
+ * or with stats[2C] when total_count is 0 (shards of any sizes).  A shard
+ * with no elements still updates running_mean / running_var.              */
 KB_API int kb_batchnorm_stats_f64(const float* x, double* stats, int64_t N,
                            int64_t C, int64_t HW, void* workspace,
                            size_t workspace_bytes, kbStream stream);

@@ -80,9 +80,11 @@ bn_stats_kernel(const float* __restrict__ x, BnShape sh, int S, bool vec,
 }
 
 // totals: stats[c] = sum, stats[C + c] = sum of squares (fp64)
+// stats = [sum (C) | sum of squares (C) | elements per channel]
 __global__ void bn_fold_kernel(const double2* __restrict__ partials, int64_t C, int S,
-                               double* __restrict__ stats) {
+                               double* __restrict__ stats, double elems) {
   const int64_t c = (int64_t)blockIdx.x * blockDim.x + threadIdx.x;
+  if (c == 0) stats[2 * C] = elems;
   if (c >= C) return;
   double s1 = 0.0, s2 = 0.0;
   for (int s = 0; s < S; ++s) {
@@ -94,8 +96,29 @@ __global__ void bn_fold_kernel(const double2* __restrict__ partials, int64_t C, 
   stats[C + c] = s2;
 }
 
+// running = (1 - momentum) * running + momentum * batch value (unbiased variance)
+__device__ __forceinline__ void bn_update_running(int64_t c, float mean, double var_d, double count,
+                                                  float momentum, float* running_mean, float* running_var) {
+  const double unbiased = count > 1.0 ? var_d * count / (count - 1.0) : var_d;
+  running_mean[c] = (1.0f - momentum) * running_mean[c] + momentum * mean;
+  running_var[c] = (1.0f - momentum) * running_var[c] + momentum * (float)unbiased;
+}
+
+// Running statistics only (a rank whose batch shard is empty still applies
+// the global batch's statistics to its copy).  count 0: stats[2C].
+__global__ void bn_running_kernel(const double* __restrict__ stats, int64_t C, int64_t count,
+                                  float momentum, float* running_mean, float* running_var) {
+  const int64_t c = (int64_t)blockIdx.x * blockDim.x + threadIdx.x;
+  if (c >= C) return;
+  const double cnt = count > 0 ? (double)count : stats[2 * C];
+  const double mean_d = stats[c] / cnt;
+  const double var_d = fmax(stats[C + c] / cnt - mean_d * mean_d, 0.0);
+  bn_update_running(c, (float)mean_d, var_d, cnt, momentum, running_mean, running_var);
+}
+
 // One CTA per (n, c) plane, planes visited in reverse order.  Channel totals
-// come from `partials` (S > 0, fixed-order fold) or from `stats` (S == 0).
+// come from `partials` (S > 0, fixed-order fold) or from `stats` (S == 0;
+// count 0: the element count stats[2C]).
 __global__ void __launch_bounds__(kThreads)
 bn_apply_kernel(const float* __restrict__ x, const float* __restrict__ gamma,
                 const float* __restrict__ beta, float* __restrict__ y, BnShape sh,
@@ -115,17 +138,15 @@ bn_apply_kernel(const float* __restrict__ x, const float* __restrict__ gamma,
     s1 = stats[c];
     s2 = stats[sh.C + c];
   }
-  const double mean_d = s1 / (double)count;
-  const double var_d = fmax(s2 / (double)count - mean_d * mean_d, 0.0);
+  const double cnt = count > 0 ? (double)count : stats[2 * sh.C];
+  const double mean_d = s1 / cnt;
+  const double var_d = fmax(s2 / cnt - mean_d * mean_d, 0.0);
   const float mean = (float)mean_d;
   const float inv_std = (float)(1.0 / sqrt(var_d + (double)eps));
   const float scale = inv_std * (gamma ? gamma[c] : 1.0f);
   const float shift = beta ? beta[c] : 0.0f;
-  if (n == 0 && threadIdx.x == 0 && running_mean && running_var) {
-    const double unbiased = count > 1 ? var_d * (double)count / (double)(count - 1) : var_d;
-    running_mean[c] = (1.0f - momentum) * running_mean[c] + momentum * mean;
-    running_var[c] = (1.0f - momentum) * running_var[c] + momentum * (float)unbiased;
-  }
+  if (n == 0 && threadIdx.x == 0 && running_mean && running_var)
+    bn_update_running(c, mean, var_d, cnt, momentum, running_mean, running_var);
   const float* xp = x + plane * sh.HW;
   float* yp = y + plane * sh.HW;
   int64_t scalar_begin = 0;
@@ -271,9 +292,10 @@ int kb_batchnorm_stats_f64(const float* x, double* stats, int64_t N, int64_t C, 
   if (N > 0) {
     kb::bn_stats_kernel<<<dim3((unsigned)C, (unsigned)S), kb::kThreads, 0, stream>>>(x, sh, S, vec, parts);
     if (int st = kb::check_launch(name)) return st;
-    kb::bn_fold_kernel<<<(unsigned)kb::ceil_div(C, 128), 128, 0, stream>>>(parts, C, S, stats);
-  } else {
-    KB_CUDA(cudaMemsetAsync(stats, 0, sizeof(double) * 2 * C, stream));
+    kb::bn_fold_kernel<<<(unsigned)kb::ceil_div(C, 128), 128, 0, stream>>>(parts, C, S, stats,
+                                                                            (double)(N * HW));
+  } else {  // an empty shard: zero sums, zero elements
+    KB_CUDA(cudaMemsetAsync(stats, 0, sizeof(double) * (2 * C + 1), stream));
   }
   return kb::check_launch(name);
 }
@@ -284,8 +306,17 @@ int kb_batchnorm_apply_f32(const float* x, const float* gamma, const float* beta
                            float* running_var, kbStream stream) {
   const char* name = "kb_batchnorm_apply_f32";
   if (int st = kb::bn_check(name, x, N, C, HW)) return st;
-  if (N * C * HW == 0) return KB_OK;
-  KB_REQUIRE(y && stats && total_count > 0, KB_ERR_INVALID_ARG, "%s: bad argument", name);
+  KB_REQUIRE(total_count >= 0 && (stats || C == 0), KB_ERR_INVALID_ARG, "%s: bad argument", name);
+  if (N * C * HW == 0) {
+    // nothing to normalise here; the running statistics still move with the global batch
+    if (C > 0 && running_mean && running_var) {
+      kb::bn_running_kernel<<<(unsigned)kb::ceil_div(C, 128), 128, 0, stream>>>(stats, C, total_count, momentum,
+                                                                                running_mean, running_var);
+      return kb::check_launch(name);
+    }
+    return KB_OK;
+  }
+  KB_REQUIRE(y, KB_ERR_INVALID_ARG, "%s: null output", name);
   const bool vec = HW % 4 == 0 && kb::aligned16(x) && kb::aligned16(y);
   kb::BnShape sh{N, C, HW};
   kb::bn_apply_kernel<<<(unsigned)(N * C), kb::kThreads, 0, stream>>>(

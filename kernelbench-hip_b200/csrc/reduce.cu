@@ -95,20 +95,25 @@ __device__ __forceinline__ double sum_partials(const double* __restrict__ p, int
   return block_sum<kThreads>(v, red);
 }
 
-// mode 0: out_f = sum / denom (fp32); mode 1: out_d = sum (fp64)
+// mode 0: out_f = sum / denom (fp32); mode 1: out_d[0] = sum (fp64), and
+// out_d[1] = elems when elems >= 0
 __global__ void __launch_bounds__(kThreads)
 finish_kernel(const double* __restrict__ partials, int count, double denom, float* out_f,
-              double* out_d) {
+              double* out_d, double elems = -1.0) {
   __shared__ double red[32];
   const double s = sum_partials(partials, count, red);
   if (threadIdx.x == 0) {
     if (out_f) out_f[0] = (float)(s / denom);
-    if (out_d) out_d[0] = s;
+    if (out_d) {
+      out_d[0] = s;
+      if (elems >= 0.0) out_d[1] = elems;
+    }
   }
 }
 
+// denom <= 0: the element count summed with the partials, total[1]
 __global__ void mse_finalize_kernel(const double* __restrict__ total, float* out, double denom) {
-  out[0] = (float)(total[0] / denom);
+  out[0] = (float)(total[0] / (denom > 0.0 ? denom : total[1]));
 }
 
 // y = x / sqrt(sumsq) with sumsq one fp64 total.  One 4096-float tile per
@@ -231,11 +236,12 @@ int kb_mse_partial_f64(const float* a, const float* b, double* partial, int64_t 
   if (n > 0) {
     if (int st = kb::launch_partials(name, a, b, n, parts, stream, &count)) return st;
   }
-  kb::finish_kernel<<<1, kb::kThreads, 0, stream>>>(parts, count, 1.0, nullptr, partial);
+  kb::finish_kernel<<<1, kb::kThreads, 0, stream>>>(parts, count, 1.0, nullptr, partial, (double)n);
   return kb::check_launch(name);
 }
 
 int kb_mse_finalize_f32(const double* total, float* out, int64_t total_n, kbStream stream) {
+  // total_n 0: divide by total[1], the shards' element counts summed with the partials
   KB_REQUIRE(total && out && total_n >= 0, KB_ERR_INVALID_ARG, "kb_mse_finalize_f32: bad argument");
   kb::mse_finalize_kernel<<<1, 1, 0, stream>>>(total, out, (double)total_n);
   return kb::check_launch("kb_mse_finalize_f32");

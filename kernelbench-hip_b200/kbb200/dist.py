@@ -23,7 +23,6 @@ gloo process group; by default they are the CUDA kernels of kbb200.ops.
 """
 from __future__ import annotations
 
-import math
 
 import torch
 import torch.distributed as tdist
@@ -74,13 +73,12 @@ def global_count(local: int, device, group=None) -> int:
 def mse_loss(a: torch.Tensor, b: torch.Tensor, total_n: int | None = None, out=None, group=None,
              kernels=None, comm=None):
     """mean((a - b)^2) over the union of all ranks' shards (replicated 0-d
-    result).  total_n defaults to world_size * a.numel() (equal shards)."""
+    result).  The element count travels with the partial sum, so shards may
+    differ in size (or be empty); total_n overrides it."""
     k = kernels or _default_kernels()
-    _, world = _world(group)
     part = k.mse_partial(a, b)
     _all_reduce_sum(part, group, comm)
-    n = total_n if total_n is not None else a.numel() * world
-    return k.mse_finalize(part, n, out=out)
+    return k.mse_finalize(part, total_n if total_n is not None else 0, out=out)
 
 
 def frobenius_normalize(x: torch.Tensor, out=None, group=None, kernels=None, comm=None):
@@ -96,13 +94,14 @@ def batch_norm_train(x: torch.Tensor, weight=None, bias=None, eps: float = 1e-5,
                      total_count: int | None = None, group=None, kernels=None, comm=None):
     """Training-mode BatchNorm with statistics over the global batch (every
     rank holds a slice of the batch dim): SyncBatchNorm semantics, equal to
-    BatchNorm on the concatenated batch."""
+    BatchNorm on the concatenated batch.  The per-channel element count is
+    summed with the statistics, so slices may differ in size; a rank with an
+    empty slice still updates its running statistics.  total_count
+    overrides the count."""
     k = kernels or _default_kernels()
-    _, world = _world(group)
     stats = k.batch_norm_stats(x)
     _all_reduce_sum(stats, group, comm)
-    per_rank = x.shape[0] * math.prod(x.shape[2:])
-    count = total_count if total_count is not None else per_rank * world
+    count = total_count if total_count is not None else 0
     return k.batch_norm_apply(x, stats, count, weight, bias, eps, momentum, running_mean,
                               running_var, out=out)
 

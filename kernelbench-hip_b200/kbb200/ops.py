@@ -252,11 +252,21 @@ def frobenius_normalize(x, out=None):
     return y
 
 
+def _f64_buffer(fn, buf, n, device):
+    """A caller's fp64 buffer of at least n contiguous elements, or a new one."""
+    if buf is None:
+        return torch.empty(n, device=device, dtype=torch.float64)
+    if buf.dtype != torch.float64 or not buf.is_contiguous() or buf.numel() < n or buf.device != device:
+        raise RuntimeError(f"{fn}: expected a contiguous float64 buffer of {n} elements on {device}")
+    return buf
+
+
 def mse_partial(a, b, partial=None):
-    """fp64 sum((a - b)^2) of this shard, for a cross-GPU sum before mse_finalize."""
+    """fp64 [sum((a - b)^2), element count] of this shard: one cross-GPU sum
+    of it gives mse_finalize both the total and the global count."""
     fn = "kb_mse_partial_f64"
     _check_f32(fn, a, b)
-    p = partial if partial is not None else torch.empty((), device=a.device, dtype=torch.float64)
+    p = _f64_buffer(fn, partial, 2, a.device)
     n = a.numel()
     ws = _workspace(a, LIB.kb_mse_workspace_size(n))
     check(fn, LIB.kb_mse_partial_f64(a.data_ptr(), b.data_ptr(), p.data_ptr(), n, ws.data_ptr(),
@@ -264,7 +274,8 @@ def mse_partial(a, b, partial=None):
     return p
 
 
-def mse_finalize(total: torch.Tensor, total_n: int, out=None):
+def mse_finalize(total: torch.Tensor, total_n: int = 0, out=None):
+    """total[0] / total_n; total_n 0: divide by the summed count total[1]."""
     fn = "kb_mse_finalize_f32"
     y = out if out is not None else torch.empty((), device=total.device, dtype=torch.float32)
     check(fn, LIB.kb_mse_finalize_f32(total.data_ptr(), y.data_ptr(), int(total_n), _stream(total)))
@@ -328,20 +339,24 @@ def batch_norm_train(x, weight=None, bias=None, eps: float = 1e-5, momentum: flo
 
 
 def batch_norm_stats(x, stats=None):
-    """fp64 [2, C] (sum, sum of squares) of this shard, for a cross-GPU sum."""
+    """fp64 [2C + 1] of this shard: per-channel sums, per-channel sums of
+    squares, elements per channel; one cross-GPU sum of it gives
+    batch_norm_apply the global statistics and count."""
     fn = "kb_batchnorm_stats_f64"
     _check_f32(fn, x)
     N, Cc = x.shape[0], x.shape[1]
     HW = math.prod(x.shape[2:])
-    st = stats if stats is not None else torch.empty((2, Cc), device=x.device, dtype=torch.float64)
+    st = _f64_buffer(fn, stats, 2 * Cc + 1, x.device)
     ws = _workspace(x, LIB.kb_batchnorm_workspace_size(N, Cc, HW))
     check(fn, LIB.kb_batchnorm_stats_f64(x.data_ptr(), st.data_ptr(), N, Cc, HW, ws.data_ptr(),
                                          ws.numel(), _stream(x)))
     return st
 
 
-def batch_norm_apply(x, stats, total_count: int, weight=None, bias=None, eps: float = 1e-5,
+def batch_norm_apply(x, stats, total_count: int = 0, weight=None, bias=None, eps: float = 1e-5,
                      momentum: float = 0.1, running_mean=None, running_var=None, out=None):
+    """Normalise with the (summed) stats of batch_norm_stats; total_count 0:
+    the element count stats[2C]."""
     fn = "kb_batchnorm_apply_f32"
     _check_f32(fn, x, weight, bias, running_mean, running_var)
     N, Cc = x.shape[0], x.shape[1]

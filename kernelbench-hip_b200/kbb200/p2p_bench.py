@@ -53,9 +53,9 @@ def main() -> int:
     comm = PeerComm(payload_bytes=1 << 20, timeout_s=10.0, device=dev)
     res = {"world": tdist.get_world_size(), "unit": "us per call", "iters": a.iters}
     try:
-        for name, n, dtype in [("mse/frobenius 8 B", 1, torch.float64),
-                               ("cross-entropy 16 B", 2, torch.float64),
-                               ("batchnorm C=128 2 KiB", 256, torch.float64),
+        for name, n, dtype in [("frobenius 8 B", 1, torch.float64),
+                               ("mse / cross-entropy 16 B", 2, torch.float64),
+                               ("batchnorm C=128 2 KiB", 257, torch.float64),
                                ("split-K C 256x256 256 KiB", 65536, torch.float32)]:
             t = torch.randn(n, dtype=dtype, device=dev)
             res[name] = {"p2p": _time(lambda: comm.all_reduce_(t), a.iters, dev),

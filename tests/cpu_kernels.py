@@ -3,16 +3,19 @@ sharding and collective composition can run on gloo ranks without a GPU.
 They follow the C-ABI contracts: fp64 partials, fp32 outputs."""
 from __future__ import annotations
 
+import math
+
 import torch
 
 
 def mse_partial(a, b):
+    """[sum((a - b)^2), element count], fp64."""
     d = a.double() - b.double()
-    return (d * d).sum().reshape(())
+    return torch.stack([(d * d).sum(), torch.tensor(float(a.numel()), dtype=torch.float64)])
 
 
-def mse_finalize(total, total_n, out=None):
-    r = (total / total_n).float()
+def mse_finalize(total, total_n=0, out=None):
+    r = (total[0] / (total_n if total_n > 0 else total[1])).float()
     if out is not None:
         out.copy_(r)
         return out
@@ -33,14 +36,18 @@ def scale_by_inv_norm(x, total, out=None):
 
 
 def batch_norm_stats(x):
+    """[sums (C), sums of squares (C), elements per channel], fp64."""
     axes = [0] + list(range(2, x.dim()))
     xd = x.double()
-    return torch.stack([xd.sum(axes), (xd * xd).sum(axes)])
+    count = x.shape[0] * math.prod(x.shape[2:])
+    return torch.cat([xd.sum(axes), (xd * xd).sum(axes), torch.tensor([float(count)], dtype=torch.float64)])
 
 
 def batch_norm_apply(x, stats, count, weight, bias, eps, momentum, running_mean, running_var, out=None):
-    mean = stats[0] / count
-    var = (stats[1] / count - mean * mean).clamp_min(0)
+    C = x.shape[1]
+    count = count if count > 0 else float(stats[2 * C])
+    mean = stats[:C] / count
+    var = (stats[C:2 * C] / count - mean * mean).clamp_min(0)
     shape = [1, -1] + [1] * (x.dim() - 2)
     y = (x.double() - mean.reshape(shape)) / torch.sqrt(var + eps).reshape(shape)
     if weight is not None:

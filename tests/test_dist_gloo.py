@@ -1,4 +1,4 @@
-"""CPU, world_size 2 (gloo): the sharded ops of kbb200.dist compose their
+"""CPU, world sizes 2, 3 and 7 (gloo): the sharded ops of kbb200.dist compose their
 per-shard partials and one collective into the same answer as the oracle on
 the whole (unsharded) input.  The per-shard kernels are the CPU stand-ins of
 tests/cpu_kernels.py; the GPU versions are the C-ABI kernels."""
@@ -42,8 +42,8 @@ def _worker(rank, world, port, case, q):
         g = torch.Generator().manual_seed(123)
         if case == "mse":
             a, b = torch.randn(10001, generator=g), torch.randn(10001, generator=g)
-            got = dist.mse_loss(dist.shard(a, rank, world), dist.shard(b, rank, world),
-                                total_n=a.numel(), kernels=CK)
+            # no total_n: the shards' element counts travel with the partial sums
+            got = dist.mse_loss(dist.shard(a, rank, world), dist.shard(b, rank, world), kernels=CK)
             want = O.mse_loss(a.numpy(), b.numpy())
             res = (float(got), float(want))
         elif case == "frobenius":
@@ -108,9 +108,15 @@ def _run(case, world=2, timeout=60):
     return out
 
 
-@pytest.mark.parametrize("case", ["mse", "frobenius", "batchnorm", "splitk", "crossentropy", "count"])
-def test_sharded_composition_matches_oracle(case):
-    out = _run(case)
+# world 3: every case has shards of unequal sizes (10001 elements, 7 / 6 / 11
+# rows, K = 1000); world 7 gives BatchNorm's 6 images an empty shard, whose
+# rank must still update its running statistics like the others
+@pytest.mark.parametrize("case,world", [(c, w) for w in (2, 3) for c in
+                                        ("mse", "frobenius", "batchnorm", "splitk", "crossentropy", "count")] +
+                         [("batchnorm", 7)])
+def test_sharded_composition_matches_oracle(case, world):
+    out = _run(case, world=world)
+    assert sorted(out) == list(range(world))
     for rank, (status, res) in out.items():
         assert status == "ok", res
         if case in ("mse", "crossentropy"):

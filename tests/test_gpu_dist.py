@@ -1,4 +1,4 @@
-"""GPU, 2 ranks over NCCL: the sharded ops of kbb200.dist with the CUDA
+"""GPU, 2 / 4 / 8 ranks over NCCL: the sharded ops of kbb200.dist with the CUDA
 per-shard kernels reproduce the single-device answer on the global input.
 
 Each rank builds the same seeded global tensors on the CPU, keeps its shard
@@ -6,7 +6,7 @@ on its own GPU, runs the sharded op (local partial kernel, one all_reduce,
 local finishing kernel) and compares with the oracle on the whole input —
 once with NCCL's all_reduce and once with the library's own all-reduce
 kernel over peer memory (kbb200.p2p.PeerComm, CUDA IPC).
-Skipped unless the process sees at least 2 GPUs.  NVLS is switched off (plain
+Each world size is skipped unless the process sees that many GPUs.  NVLS is switched off (plain
 NCCL rings over NVLink).
 """
 from __future__ import annotations
@@ -63,9 +63,16 @@ def _worker(rank, world, port, q):
 
         x = torch.randn(6, 32, 20, 24, generator=g) * 2 + 1
         w, bb = 1 + 0.02 * torch.randn(32, generator=g), 0.02 * torch.randn(32, generator=g)
-        got = dist.batch_norm_train(dist.shard(x, rank, world).to(dev), w.to(dev), bb.to(dev)).cpu().numpy()
+        xs_bn = dist.shard(x, rank, world).to(dev)
+        rm, rv = torch.zeros(32, device=dev), torch.ones(32, device=dev)
+        got = dist.batch_norm_train(xs_bn, w.to(dev), bb.to(dev), 1e-5, 0.1, rm, rv).cpu().numpy()
         lo, hi = dist.shard_range(6, rank, world)
-        res["batchnorm"] = (got, O.batch_norm_train(x.numpy(), w.numpy(), bb.numpy())[lo:hi], 1e-5)
+        want_bn = O.batch_norm_train(x.numpy(), w.numpy(), bb.numpy())[lo:hi]
+        res["batchnorm"] = (got, want_bn, 1e-5)
+        erm, erv = O.batch_norm_running_update(x.numpy(), np.zeros(32), np.ones(32))
+        res["batchnorm_running_mean"] = (rm.cpu().numpy(), erm, 1e-5)   # empty shards too
+        res["batchnorm_running_var"] = (rv.cpu().numpy(), erv, 1e-5)
+        x_bn, w_bn, b_bn = x, w, bb
 
         A, B = torch.randn(256, 65536, generator=g), torch.randn(65536, 256, generator=g)
         As = dist.shard(A, rank, world, dim=1).contiguous().to(dev)
@@ -95,6 +102,8 @@ def _worker(rank, world, port, q):
             res["p2p_frobenius"] = (got, O.frobenius_normalize(x0.numpy())[lo0:hi0], 1e-5)
             got = dist.cross_entropy(lgs, tgs, comm=comm)
             res["p2p_cross_entropy"] = (float(got), want_ce, 1e-5)
+            got = dist.batch_norm_train(xs_bn, w_bn.to(dev), b_bn.to(dev), comm=comm).cpu().numpy()
+            res["p2p_batchnorm"] = (got, want_bn, 1e-5)
             c1 = dist.matmul_splitk(As, Bs, comm=comm)
             c2 = dist.matmul_splitk(As, Bs, comm=comm)
             res["p2p_splitk"] = (c1.cpu().numpy(), want_c, 1e-3)
@@ -113,10 +122,12 @@ def _worker(rank, world, port, q):
         q.put((rank, "err", f"{type(e).__name__}: {e}\n{traceback.format_exc()[-600:]}"))
 
 
-def test_sharded_ops_on_two_gpus():
-    if torch.cuda.device_count() < 2:
-        pytest.skip("needs 2 GPUs")
-    world = 2
+# 4 and 8 ranks give uneven shards (BatchNorm's 6 images: 2/2/1/1, and two
+# empty shards at 8) and exercise the peer all-reduce with more than one peer
+@pytest.mark.parametrize("world", [2, 4, 8])
+def test_sharded_ops_on_several_gpus(world):
+    if torch.cuda.device_count() < world:
+        pytest.skip(f"needs {world} GPUs")
     ctx = mp.get_context("spawn")
     q = ctx.Queue()
     port = _free_port()
