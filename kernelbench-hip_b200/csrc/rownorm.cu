@@ -188,6 +188,17 @@ __device__ __forceinline__ void store_row(float4* yrow, const float4 (&v)[VPT], 
   }
 }
 
+// 2^x by the hardware's ex2.approx.ftz instruction (PTX ISA); results below
+// 2^-126 become 0 instead of subnormal.  For the per-element softmax
+// exponentials such terms are below fp32 resolution after the division by
+// the row sum (or in the log of the sum); 1 % faster at 8192 x 32768 than
+// exp2f, identical outputs on N(0, 4) rows.
+__device__ __forceinline__ float ex2_ftz(float x) {
+  float y;
+  asm("ex2.approx.ftz.f32 %0, %1;" : "=f"(y) : "f"(x));
+  return y;
+}
+
 template <RowOp OP, int VPT, bool PAIRED = false, class R>
 __device__ __forceinline__ void row_math(float4 (&v)[VPT], const bool (&ok)[VPT],
                                          const RowArgs& a, float4* yrow, int64_t col4_base,
@@ -267,10 +278,10 @@ __device__ __forceinline__ void row_math(float4 (&v)[VPT], const bool (&ok)[VPT]
 #pragma unroll
       for (int k = 0; k < VPT; ++k)
         if (ok[k]) {
-          v[k].x = exp2f(fmaf(v[k].x, kLog2e, -mtl));
-          v[k].y = exp2f(fmaf(v[k].y, kLog2e, -mtl));
-          v[k].z = exp2f(fmaf(v[k].z, kLog2e, -mtl));
-          v[k].w = exp2f(fmaf(v[k].w, kLog2e, -mtl));
+          v[k].x = ex2_ftz(fmaf(v[k].x, kLog2e, -mtl));
+          v[k].y = ex2_ftz(fmaf(v[k].y, kLog2e, -mtl));
+          v[k].z = ex2_ftz(fmaf(v[k].z, kLog2e, -mtl));
+          v[k].w = ex2_ftz(fmaf(v[k].w, kLog2e, -mtl));
           st += (v[k].x + v[k].y) + (v[k].z + v[k].w);
         }
       const MaxSum tot = red.maxsum(MaxSum{mt, st}, 0);
@@ -282,8 +293,8 @@ __device__ __forceinline__ void row_math(float4 (&v)[VPT], const bool (&ok)[VPT]
 #pragma unroll
       for (int k = 0; k < VPT; ++k)
         if (ok[k])
-          st += (exp2f(fmaf(v[k].x, kLog2e, -mtl)) + exp2f(fmaf(v[k].y, kLog2e, -mtl))) +
-                (exp2f(fmaf(v[k].z, kLog2e, -mtl)) + exp2f(fmaf(v[k].w, kLog2e, -mtl)));
+          st += (ex2_ftz(fmaf(v[k].x, kLog2e, -mtl)) + ex2_ftz(fmaf(v[k].y, kLog2e, -mtl))) +
+                (ex2_ftz(fmaf(v[k].z, kLog2e, -mtl)) + ex2_ftz(fmaf(v[k].w, kLog2e, -mtl)));
       const MaxSum tot = red.maxsum(MaxSum{mt, st}, 0);
       // (x - max) - log sum, in this order: x - (max + log sum) is 2 % faster
       // but rounds max + log sum at max's magnitude (|max| ~ 1e4 gave errors
