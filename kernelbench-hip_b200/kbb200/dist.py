@@ -7,9 +7,10 @@ real exchange step, and each takes exactly one collective between a local
 partial kernel and a local finishing kernel (the split C-ABI entry pairs):
 
     op                 local partial            collective            finish
-    mse_loss           sum (a-b)^2  (fp64)      all_reduce 8 B        divide by total count
+    mse_loss           sum (a-b)^2, count       all_reduce 16 B       divide by total count
     frobenius          sum x^2      (fp64)      all_reduce 8 B        x / sqrt(total)
-    batch_norm_train   per-channel sum, sum^2   all_reduce 16*C B     normalise + affine
+    batch_norm_train   per-channel sum, sum^2,  all_reduce 16*C+8 B   normalise + affine
+                       count
     cross_entropy      sum of losses, count     all_reduce 16 B       divide
     matmul_splitk      partial C over K slice   all_reduce M*N*4 B    (result replicated)
 
@@ -17,7 +18,11 @@ The collective is either torch.distributed's all_reduce (NCCL over NVLink on
 B200s; gloo on CPU) or, given `comm=PeerComm(...)` (kbb200.p2p), the
 library's own all-reduce kernel over peer memory; for split-K that kernel
 also performs the rank's own K-split reduction, so local finish and
-cross-GPU sum are one launch.  The per-shard kernels are injectable
+cross-GPU sum are one launch.  The peer kernel pushes each rank's payload to
+every peer, so it wins where the exchange is latency-bound: it is used on 2
+ranks for every payload and on more ranks for payloads of at most
+PEER_MAX_BYTES; larger exchanges on more ranks go to NCCL even when a
+PeerComm is given (see peer_path).  The per-shard kernels are injectable
 (`kernels=`) so the composition can be tested with CPU implementations on a
 gloo process group; by default they are the CUDA kernels of kbb200.ops.
 """
@@ -53,8 +58,23 @@ def shard(t: torch.Tensor, rank: int, world: int, dim: int = 0) -> torch.Tensor:
     return t.narrow(dim, lo, hi - lo)
 
 
+# Measured on B200s (µs per call, peer kernel vs NCCL all_reduce, NVLS off):
+# 2 ranks 10.5-15.1 vs 18.8-31.5 from 8 B to 2 KiB and 17.6 vs 18.8 at
+# 256 KiB; 4 ranks 14.9 / 15.3 vs 19.9 / 19.0 at 8 / 16 B, but 21.5 vs 17.7
+# at 2 KiB and 30.7 vs 19.5 at 256 KiB (every rank's pushes grow with the
+# world size, NCCL's ring traffic does not).
+PEER_MAX_BYTES = 64
+
+
+def peer_path(comm, nbytes: int) -> bool:
+    """Whether an exchange of nbytes per rank goes through the PeerComm.
+    Every rank passes the same nbytes and world size, so all ranks take the
+    same path and the collective order stays identical."""
+    return comm is not None and (comm.world <= 2 or nbytes <= PEER_MAX_BYTES)
+
+
 def _all_reduce_sum(t: torch.Tensor, group=None, comm=None) -> torch.Tensor:
-    if comm is not None:
+    if peer_path(comm, t.numel() * t.element_size()):
         return comm.all_reduce_(t)
     if _world(group)[1] > 1:
         tdist.all_reduce(t, op=tdist.ReduceOp.SUM, group=group)
@@ -110,10 +130,11 @@ def matmul_splitk(a: torch.Tensor, b: torch.Tensor, out=None, group=None, kernel
     """C = A @ B with K sharded: rank r holds A[:, K_r] and B[K_r, :].  Each
     rank computes its partial C (split-K across its own SMs as well), then one
     all_reduce sums the partials; every rank ends with the full C.  With a
-    PeerComm the rank's K-split tiles go straight into the peer all-reduce
-    kernel, which sums them (split order) and then across ranks (rank order)."""
+    PeerComm on 2 ranks (or a C of at most PEER_MAX_BYTES) the rank's K-split
+    tiles go straight into the peer all-reduce kernel, which sums them (split
+    order) and then across ranks (rank order)."""
     k = kernels or _default_kernels()
-    if comm is not None:
+    if peer_path(comm, a.shape[0] * b.shape[1] * 4):
         parts, splits = k.matmul_splitk_partials(a, b)
         c = out if out is not None else torch.empty(a.shape[0], b.shape[1], device=a.device,
                                                     dtype=torch.float32)

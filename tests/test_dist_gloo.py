@@ -149,3 +149,17 @@ def test_shard_range_partitions_exactly():
             assert all(spans[i][1] == spans[i + 1][0] for i in range(w - 1))
             sizes = [h - l for l, h in spans]
             assert max(sizes) - min(sizes) <= 1
+
+
+def test_peer_path_routing():
+    """The peer all-reduce serves every payload on 2 ranks and only small
+    ones (latency-bound) on more ranks; without a PeerComm it is never used."""
+    from types import SimpleNamespace
+
+    from kbb200.dist import PEER_MAX_BYTES, peer_path
+
+    two, four, eight = (SimpleNamespace(world=w) for w in (2, 4, 8))
+    assert peer_path(two, 8) and peer_path(two, 256 * 1024)
+    assert peer_path(four, 16) and peer_path(eight, PEER_MAX_BYTES)
+    assert not peer_path(four, PEER_MAX_BYTES + 1) and not peer_path(eight, 256 * 1024)
+    assert not peer_path(None, 8)
