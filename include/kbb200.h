@@ -170,9 +170,11 @@ KB_API int kb_batchnorm_train_f32(const float* x, const float* gamma,
  * live in a 128 KiB file-scope device array (8192 fp64 pairs) that every
  * device loading the library keeps until process exit, so C * splits must be
  * <= 8192, where splits = max(1, min(N, ceil(4 * SMs / C))), so any
- * C <= 8192 fits on a 148-SM B200.  Larger C returns KB_ERR_UNSUPPORTED.  The first
- * call on a device looks up the array's device address
- * (cudaGetSymbolAddress); make it before any stream capture.  Every call
+ * C <= 8192 fits on a 148-SM B200.  Larger C returns KB_ERR_UNSUPPORTED.  Each
+ * call looks up the array's device address on the current device
+ * (cudaGetSymbolAddress), so the address stays valid across a
+ * cudaDeviceReset; the first call on a device also loads the module there,
+ * so make it before any stream capture.  Every call
  * shares the one array, so calls that overlap on the GPU (for example on two
  * streams) race; the caller must serialise them.  Calls no cudaMalloc.     */
 KB_API int kb_batchnorm_train_f32_noalloc(const float* x, const float* gamma,
@@ -272,7 +274,7 @@ KB_API int kb_cross_entropy_finalize_f32(const double* total, float* out, kbStre
  *            dst = sum over ranks of src (rank order: bit-identical on all
  *            ranks).  src may equal dst.
  *   failure  a wait longer than timeout_ns records (phase << 8 | peer) in
- *            the fault word (kb_p2p_read_fault) and leaves dst unwritten;
+ *            the fault word (kb_p2p_read_fault) and writes NaN into dst;
  *            the buffer set must then be discarded.                       */
 KB_API size_t kb_p2p_header_bytes(void);
 KB_API size_t kb_p2p_buffer_bytes(size_t payload_bytes, int world);
@@ -298,6 +300,42 @@ KB_API int kb_p2p_splitk_allreduce_f32(void* const* bufs, int rank, int world,
                                 int splits, float* dst, int64_t n,
                                 unsigned epoch, uint64_t timeout_ns,
                                 kbStream stream);
+/* Fused sharded reductions, one launch each: this rank's partial pass, a
+ * fixed-order fold by the CTA that finishes last, and that CTA's exchange
+ * of the folded values over the peer buffers (same buffers, epochs and
+ * fault word as kb_p2p_allreduce_*; a call takes one epoch).  They replace
+ * the three to four launches of partial entry + all-reduce + finish entry
+ * of the sharded MSE, Frobenius and BatchNorm (replaced reference entries:
+ * mse_entry, candidates/94_MSELoss/v1.py:35-45; fro_entry,
+ * candidates/37_FrobeniusNorm_/v1.py:48-58; bn_entry,
+ * candidates/33_BatchNorm/v1.py:53-68).  The workspace begins with a
+ * 256-byte arrival counter that must be zero before the first call; every
+ * call leaves it zero, so one zeroed workspace serves every call of a
+ * stream.  On an expired wait the results are NaN and the fault word is
+ * set.
+ *   kb_mse_sharded_f32      out = sum over ranks of sum (a-b)^2 / sum over
+ *                           ranks of n (shards of any size, empty too)
+ *   kb_sumsq_sharded_f64    total = sum over ranks of sum x^2; then
+ *                           kb_scale_by_inv_norm_f32 on the shard
+ *   kb_batchnorm_stats_sharded_f64   stats[2C + 1] = global per-channel
+ *                           sums, sums of squares and elements per channel;
+ *                           then kb_batchnorm_apply_f32 on the shard      */
+KB_API size_t kb_sharded_workspace_size(void);
+KB_API int kb_mse_sharded_f32(const float* a, const float* b, float* out, int64_t n,
+                              void* workspace, size_t workspace_bytes, void* const* bufs,
+                              int rank, int world, size_t buf_bytes, unsigned epoch,
+                              uint64_t timeout_ns, kbStream stream);
+KB_API int kb_sumsq_sharded_f64(const float* x, double* total, int64_t n, void* workspace,
+                                size_t workspace_bytes, void* const* bufs, int rank,
+                                int world, size_t buf_bytes, unsigned epoch,
+                                uint64_t timeout_ns, kbStream stream);
+KB_API size_t kb_batchnorm_sharded_workspace_size(int64_t N, int64_t C, int64_t HW);
+KB_API int kb_batchnorm_stats_sharded_f64(const float* x, double* stats, int64_t N,
+                                          int64_t C, int64_t HW, void* workspace,
+                                          size_t workspace_bytes, void* const* bufs,
+                                          int rank, int world, size_t buf_bytes,
+                                          unsigned epoch, uint64_t timeout_ns,
+                                          kbStream stream);
 /* the K-split partial tiles of C = A[M,K] B[K,N] without their reduction:
  * workspace[z][M][N] for z < *splits.                                     */
 KB_API size_t kb_gemm_splitk_partials_workspace_size(int64_t M, int64_t N, int64_t K);

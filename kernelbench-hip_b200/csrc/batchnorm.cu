@@ -10,9 +10,9 @@
 // derives mean / inv-std in fp64 and writes y = (x - mean) * (inv_std * gamma)
 // + beta.  x is read twice (2 GiB does not fit on chip); planes are applied in
 // reverse order so the first ones still sit in L2 from the end of pass 1.
-#include <mutex>
 
 #include "kb_common.cuh"
+#include "peer_exchange.cuh"
 
 namespace kb {
 namespace {
@@ -77,6 +77,39 @@ bn_stats_kernel(const float* __restrict__ x, BnShape sh, int S, bool vec,
   s1 = block_sum<kThreads>(s1, red);
   s2 = block_sum<kThreads>(s2, red);
   if (threadIdx.x == 0) partials[c * S + s] = make_double2(s1, s2);
+}
+
+// Sharded form of the statistics pass: the grid and partials of
+// bn_stats_kernel; the CTA that arrives last folds every channel's S
+// partials in split order into stats = [sum (C) | sum of squares (C) |
+// elements per channel], then exchanges those 2C + 1 values with every rank
+// over the peer buffers (peer_exchange.cuh): stats ends as the global totals.
+__global__ void __launch_bounds__(kThreads)
+bn_stats_sharded_kernel(const float* __restrict__ x, BnShape sh, int S, bool vec, double2* __restrict__ partials,
+                        unsigned* counter, PeerCtx peer, double* __restrict__ stats) {
+  __shared__ double red[32];
+  const int64_t c = blockIdx.x;
+  const int s = blockIdx.y;
+  const int64_t n0 = sh.N * s / S, n1 = sh.N * (s + 1) / S;
+  double s1 = 0.0, s2 = 0.0;
+  for (int64_t n = n0; n < n1; ++n) plane_sums(x + (n * sh.C + c) * sh.HW, sh.HW, vec, s1, s2);
+  s1 = block_sum<kThreads>(s1, red);
+  s2 = block_sum<kThreads>(s2, red);
+  if (threadIdx.x == 0) partials[c * S + s] = make_double2(s1, s2);
+  if (!last_cta_arrives(counter)) return;
+  for (int64_t ch = threadIdx.x; ch < sh.C; ch += kThreads) {
+    double t1 = 0.0, t2 = 0.0;
+    for (int z = 0; z < S; ++z) {
+      const double2 p = __ldcg(partials + ch * S + z);
+      t1 += p.x;
+      t2 += p.y;
+    }
+    stats[ch] = t1;
+    stats[sh.C + ch] = t2;
+  }
+  if (threadIdx.x == 0) stats[2 * sh.C] = (double)(sh.N * sh.HW);
+  __syncthreads();
+  block_peer_allreduce(peer, stats, stats, (int)(2 * sh.C + 1));
 }
 
 // totals: stats[c] = sum, stats[C + c] = sum of squares (fp64)
@@ -181,30 +214,22 @@ bn_apply_kernel(const float* __restrict__ x, const float* __restrict__ gamma,
 // Allocation-free variant: the per-channel partials live in this file-scope
 // device array instead of caller workspace.  Every device that loads the
 // library holds it until exit.  Host code must not pass the symbol itself to a
-// kernel (on the host it is only a stand-in, not a device address); the
-// device address is looked up once per device with cudaGetSymbolAddress.
+// kernel (on the host it is only a stand-in, not a device address): each call
+// looks the device address up on the current device with cudaGetSymbolAddress
+// (cheap next to the two launches), so the address stays right when the
+// module is loaded again after a cudaDeviceReset.  The first call on a device
+// loads the module there and should come before any stream capture.
 // ---------------------------------------------------------------------------
 constexpr int kNoAllocPartials = 8192;  // (sum, sum of squares) pairs: 128 KiB
 static __device__ __align__(256) double2 g_bn_noalloc_partials[kNoAllocPartials];
 
-std::mutex g_noalloc_mu;
-double2* g_noalloc_ptr[64] = {};
-
-// Device address of g_bn_noalloc_partials on the current device; the first
-// call on a device performs the lookup.
+// Device address of g_bn_noalloc_partials on the current device.
 int noalloc_partials(double2** out) {
-  int dev = 0;
-  KB_CUDA(cudaGetDevice(&dev));
-  KB_REQUIRE(dev >= 0 && dev < 64, KB_ERR_DEVICE, "device ordinal %d out of range", dev);
-  std::lock_guard<std::mutex> lock(g_noalloc_mu);
-  if (g_noalloc_ptr[dev] == nullptr) {
-    void* p = nullptr;
-    const cudaError_t e = cudaGetSymbolAddress(&p, g_bn_noalloc_partials);
-    if (e != cudaSuccess || p == nullptr)
-      return set_error(KB_ERR_CUDA, "cudaGetSymbolAddress(batchnorm scratch): %s", cudaGetErrorString(e));
-    g_noalloc_ptr[dev] = static_cast<double2*>(p);
-  }
-  *out = g_noalloc_ptr[dev];
+  void* p = nullptr;
+  const cudaError_t e = cudaGetSymbolAddress(&p, g_bn_noalloc_partials);
+  if (e != cudaSuccess || p == nullptr)
+    return set_error(KB_ERR_CUDA, "cudaGetSymbolAddress(batchnorm scratch): %s", cudaGetErrorString(e));
+  *out = static_cast<double2*>(p);
   return KB_OK;
 }
 
@@ -297,6 +322,40 @@ int kb_batchnorm_stats_f64(const float* x, double* stats, int64_t N, int64_t C, 
   } else {  // an empty shard: zero sums, zero elements
     KB_CUDA(cudaMemsetAsync(stats, 0, sizeof(double) * (2 * C + 1), stream));
   }
+  return kb::check_launch(name);
+}
+
+size_t kb_batchnorm_sharded_workspace_size(int64_t N, int64_t C, int64_t HW) {
+  return kb::kShardedCounterBytes + kb_batchnorm_workspace_size(N, C, HW);
+}
+
+int kb_batchnorm_stats_sharded_f64(const float* x, double* stats, int64_t N, int64_t C, int64_t HW,
+                                   void* workspace, size_t workspace_bytes, void* const* bufs, int rank,
+                                   int world, size_t buf_bytes, unsigned epoch, uint64_t timeout_ns,
+                                   kbStream stream) {
+  const char* name = "kb_batchnorm_stats_sharded_f64";
+  if (int st = kb::bn_check(name, x, N, C, HW)) return st;
+  KB_REQUIRE(C > 0 && stats, KB_ERR_INVALID_ARG, "%s: no channels or null stats", name);
+  KB_REQUIRE(C <= 65535, KB_ERR_UNSUPPORTED, "%s: more than 65535 channels", name);
+  KB_REQUIRE(workspace && workspace_bytes >= kb_batchnorm_sharded_workspace_size(N, C, HW), KB_ERR_WORKSPACE,
+             "%s: workspace of %zu bytes needed", name, kb_batchnorm_sharded_workspace_size(N, C, HW));
+  KB_REQUIRE((reinterpret_cast<uintptr_t>(workspace) & 255) == 0, KB_ERR_INVALID_ARG,
+             "%s: workspace must be 256-byte aligned", name);
+  KB_REQUIRE(bufs && world >= 1 && world <= kb::kPeerMaxRanks && rank >= 0 && rank < world && epoch != 0,
+             KB_ERR_INVALID_ARG, "%s: bad communicator (rank %d of %d, epoch %u)", name, rank, world, epoch);
+  const size_t cap = kb::p2p_part_cap(buf_bytes, world);
+  KB_REQUIRE((size_t)(2 * C + 1) * sizeof(double) <= cap, KB_ERR_WORKSPACE,
+             "%s: %lld-value exchange exceeds the %zu-byte slot", name, (long long)(2 * C + 1), cap);
+  int* fault = nullptr;
+  if (int st = kb::p2p_fault_address(&fault)) return st;
+  const kb::PeerCtx peer{reinterpret_cast<char* const*>(bufs), rank, world, cap, epoch, timeout_ns, fault};
+  const int S = kb::bn_splits(N, C);
+  const bool vec = HW % 4 == 0 && kb::aligned16(x);
+  unsigned* counter = static_cast<unsigned*>(workspace);
+  double2* parts = reinterpret_cast<double2*>(static_cast<char*>(workspace) + kb::kShardedCounterBytes);
+  kb::BnShape sh{N, C, HW};
+  kb::bn_stats_sharded_kernel<<<dim3((unsigned)C, (unsigned)S), kb::kThreads, 0, stream>>>(x, sh, S, vec, parts,
+                                                                                          counter, peer, stats);
   return kb::check_launch(name);
 }
 

@@ -25,11 +25,14 @@
 // e + 2, after its call e + 1 saw every rank's signal, which each rank sends
 // only after its call e (and so its reads of slot e & 1) completed.
 // Every wait is bounded by %globaltimer; on expiry the kernel records a
-// fault word (kb_p2p_read_fault), leaves without writing dst, and the buffer
-// set must be discarded (its barrier state is no longer consistent).
+// fault word (kb_p2p_read_fault), fills dst with NaN (an in-place call would
+// otherwise leave this rank's own partial there, a plausible wrong answer),
+// and the buffer set must be discarded (its barrier state is no longer
+// consistent).
 #include <string.h>
 
 #include "kb_common.cuh"
+#include "peer_exchange.cuh"
 
 namespace kb {
 
@@ -160,11 +163,14 @@ __global__ void __launch_bounds__(kP2PThreads) p2p_allreduce_kernel(P2PArgs a) {
     s_ok = ok ? 1 : 0;
   }
   __syncthreads();
-  if (!s_ok) return;
+  T* dst = static_cast<T*>(a.dst);
+  if (!s_ok) {  // an expired wait: NaN, so a failed exchange cannot pass for a local result
+    for (int64_t i = i0; i < a.n; i += stride) dst[i] = T(NAN);
+    return;
+  }
   __threadfence_system();
 
   // 5. rank-ordered sum of the parts that arrived in this rank's slot
-  T* dst = static_cast<T*>(a.dst);
   const char* own = a.bufs[a.rank];
   for (int64_t i = i0; i < a.n; i += stride) {
     T acc = T(0);
@@ -207,6 +213,21 @@ size_t part_cap(size_t buf_bytes, int world) {
 }
 
 }  // namespace
+
+// For the fused sharded kernels (peer_exchange.cuh): they share this file's
+// fault word, read through its device address, and its slot layout.
+int p2p_fault_address(int** out) {
+  void* p = nullptr;
+  KB_CUDA(cudaGetSymbolAddress(&p, g_p2p_fault));
+  *out = static_cast<int*>(p);
+  return KB_OK;
+}
+
+size_t p2p_part_cap(size_t buf_bytes, int world) { return part_cap(buf_bytes, world); }
+
+static_assert(kHeaderBytes == kPeerHeaderBytes && kMaxRanks == kPeerMaxRanks && sizeof(Header) == sizeof(PeerHeader),
+              "peer_exchange.cuh and p2p.cu must agree on the buffer layout");
+
 }  // namespace kb
 
 extern "C" {

@@ -16,6 +16,7 @@
 // end backwards so that its first tiles are the ones the sum pass touched
 // last, still resident in the 126 MB L2.
 #include "kb_common.cuh"
+#include "peer_exchange.cuh"
 
 namespace kb {
 namespace {
@@ -29,12 +30,11 @@ int reduce_grid(int64_t nvec) {
   return (int)std::max<int64_t>(1, std::min<int64_t>({want, (int64_t)sm_count() * 4, (int64_t)kMaxPartials}));
 }
 
-// sum over i of f(a[i], b[i]) -> partials[blockIdx.x]
+// This thread's share of sum over i of f(a[i], b[i]) (f = (a - b)^2 or a^2)
+// over a grid-stride walk of 1024-float4 tiles.
 template <bool DIFF>
-__global__ void __launch_bounds__(kThreads)
-sq_partial_kernel(const float* __restrict__ a, const float* __restrict__ b, int64_t n,
-                  bool vec, double* __restrict__ partials) {
-  __shared__ double red[32];
+__device__ __forceinline__ double sq_thread_sum(const float* __restrict__ a, const float* __restrict__ b,
+                                                int64_t n, bool vec) {
   double dacc = 0.0;
   int64_t scalar_begin = 0;
   if (vec) {
@@ -83,8 +83,47 @@ sq_partial_kernel(const float* __restrict__ a, const float* __restrict__ b, int6
     if constexpr (DIFF) d -= b[i];
     dacc += (double)(d * d);
   }
-  const double tot = block_sum<kThreads>(dacc, red);
+  return dacc;
+}
+
+// sum over i of f(a[i], b[i]) -> partials[blockIdx.x]
+template <bool DIFF>
+__global__ void __launch_bounds__(kThreads)
+sq_partial_kernel(const float* __restrict__ a, const float* __restrict__ b, int64_t n,
+                  bool vec, double* __restrict__ partials) {
+  __shared__ double red[32];
+  const double tot = block_sum<kThreads>(sq_thread_sum<DIFF>(a, b, n, vec), red);
   if (threadIdx.x == 0) partials[blockIdx.x] = tot;
+}
+
+// Sharded form, one launch: the partials of this rank's shard; the CTA that
+// arrives last folds them in a fixed order and exchanges the fold with every
+// rank over the peer buffers (peer_exchange.cuh).  MSE (DIFF): the exchange
+// carries (sum, element count) and out_f[0] = global sum / global count;
+// sum of squares: out_d[0] = the global sum.
+template <bool DIFF>
+__global__ void __launch_bounds__(kThreads)
+sq_sharded_kernel(const float* __restrict__ a, const float* __restrict__ b, int64_t n, bool vec,
+                  double* __restrict__ partials, unsigned* counter, PeerCtx peer, float* out_f,
+                  double* out_d) {
+  __shared__ double red[32];
+  __shared__ double vals[2];
+  const double tot = block_sum<kThreads>(sq_thread_sum<DIFF>(a, b, n, vec), red);
+  if (threadIdx.x == 0) partials[blockIdx.x] = tot;
+  if (!last_cta_arrives(counter)) return;
+  double v = 0.0;
+  for (int i = threadIdx.x; i < (int)gridDim.x; i += kThreads) v += __ldcg(partials + i);
+  v = block_sum<kThreads>(v, red);
+  if (threadIdx.x == 0) {
+    vals[0] = v;
+    vals[1] = (double)n;
+  }
+  __syncthreads();
+  block_peer_allreduce(peer, vals, vals, DIFF ? 2 : 1);
+  if (threadIdx.x == 0) {
+    if (out_f) out_f[0] = (float)(vals[0] / vals[1]);
+    if (out_d) out_d[0] = vals[0];
+  }
 }
 
 // Fixed-order sum of `count` fp64 partials by one CTA (identical in every
@@ -202,10 +241,67 @@ int launch_partials(const char* name, const float* a, const float* b, int64_t n,
   return check_launch(name);
 }
 
+// the peer view of one call of a fused sharded entry; checks the payload fits a slot
+int make_peer(const char* name, void* const* bufs, int rank, int world, size_t buf_bytes, unsigned epoch,
+              uint64_t timeout_ns, size_t payload_bytes, PeerCtx* out) {
+  KB_REQUIRE(bufs && world >= 1 && world <= kPeerMaxRanks && rank >= 0 && rank < world, KB_ERR_INVALID_ARG,
+             "%s: bad communicator (rank %d of %d)", name, rank, world);
+  KB_REQUIRE(epoch != 0, KB_ERR_INVALID_ARG, "%s: epoch 0 is reserved", name);
+  const size_t cap = p2p_part_cap(buf_bytes, world);
+  KB_REQUIRE(payload_bytes <= cap, KB_ERR_WORKSPACE, "%s: %zu-byte exchange exceeds the %zu-byte slot", name,
+             payload_bytes, cap);
+  int* fault = nullptr;
+  if (int st = p2p_fault_address(&fault)) return st;
+  *out = PeerCtx{reinterpret_cast<char* const*>(bufs), rank, world, cap, epoch, timeout_ns, fault};
+  return KB_OK;
+}
+
+// a sharded entry's workspace: the arrival counter (first 256 bytes), then
+// the per-CTA partials
+constexpr size_t kShardedWorkspace = kShardedCounterBytes + kMaxPartials * sizeof(double);
+
+int launch_sharded(const char* name, const float* a, const float* b, int64_t n, void* ws, size_t ws_bytes,
+                   const PeerCtx& peer, float* out_f, double* out_d, cudaStream_t s) {
+  if (int st = check_ws(name, ws, ws_bytes, kShardedWorkspace)) return st;
+  unsigned* counter = static_cast<unsigned*>(ws);
+  double* parts = reinterpret_cast<double*>(static_cast<char*>(ws) + kShardedCounterBytes);
+  const bool vec = n > 0 && aligned16(a) && (!b || aligned16(b));
+  const int grid = n > 0 ? reduce_grid(vec ? n / 4 : n) : 1;
+  if (b) sq_sharded_kernel<true><<<grid, kThreads, 0, s>>>(a, b, n, vec, parts, counter, peer, out_f, out_d);
+  else sq_sharded_kernel<false><<<grid, kThreads, 0, s>>>(a, nullptr, n, vec, parts, counter, peer, out_f, out_d);
+  return check_launch(name);
+}
+
 }  // namespace
 }  // namespace kb
 
 extern "C" {
+
+size_t kb_sharded_workspace_size(void) { return kb::kShardedWorkspace; }
+
+int kb_mse_sharded_f32(const float* a, const float* b, float* out, int64_t n, void* workspace,
+                       size_t workspace_bytes, void* const* bufs, int rank, int world, size_t buf_bytes,
+                       unsigned epoch, uint64_t timeout_ns, kbStream stream) {
+  const char* name = "kb_mse_sharded_f32";
+  KB_REQUIRE(n >= 0, KB_ERR_INVALID_ARG, "%s: negative n", name);
+  KB_REQUIRE(out && (n == 0 || (a && b)), KB_ERR_INVALID_ARG, "%s: null pointer", name);
+  kb::PeerCtx peer;
+  if (int st = kb::make_peer(name, bufs, rank, world, buf_bytes, epoch, timeout_ns, 2 * sizeof(double), &peer))
+    return st;
+  return kb::launch_sharded(name, a, b, n, workspace, workspace_bytes, peer, out, nullptr, stream);
+}
+
+int kb_sumsq_sharded_f64(const float* x, double* total, int64_t n, void* workspace, size_t workspace_bytes,
+                         void* const* bufs, int rank, int world, size_t buf_bytes, unsigned epoch,
+                         uint64_t timeout_ns, kbStream stream) {
+  const char* name = "kb_sumsq_sharded_f64";
+  KB_REQUIRE(n >= 0, KB_ERR_INVALID_ARG, "%s: negative n", name);
+  KB_REQUIRE(total && (n == 0 || x), KB_ERR_INVALID_ARG, "%s: null pointer", name);
+  kb::PeerCtx peer;
+  if (int st = kb::make_peer(name, bufs, rank, world, buf_bytes, epoch, timeout_ns, sizeof(double), &peer))
+    return st;
+  return kb::launch_sharded(name, x, nullptr, n, workspace, workspace_bytes, peer, nullptr, total, stream);
+}
 
 size_t kb_mse_workspace_size(int64_t) { return kb::kMaxPartials * sizeof(double); }
 

@@ -77,6 +77,12 @@ SIGNATURES: dict[str, tuple] = {
     "kb_p2p_allreduce_f32": (_int, [_p, _int, _int, _sz, _p, _p, _i64, C.c_uint, C.c_uint64, _p]),
     "kb_p2p_splitk_allreduce_f32": (_int, [_p, _int, _int, _sz, _p, _int, _p, _i64, C.c_uint, C.c_uint64,
                                            _p]),
+    "kb_sharded_workspace_size": (_sz, []),
+    "kb_mse_sharded_f32": (_int, [_p, _p, _p, _i64, _p, _sz, _p, _int, _int, _sz, C.c_uint, C.c_uint64, _p]),
+    "kb_sumsq_sharded_f64": (_int, [_p, _p, _i64, _p, _sz, _p, _int, _int, _sz, C.c_uint, C.c_uint64, _p]),
+    "kb_batchnorm_sharded_workspace_size": (_sz, [_i64, _i64, _i64]),
+    "kb_batchnorm_stats_sharded_f64": (_int, [_p, _p, _i64, _i64, _i64, _p, _sz, _p, _int, _int, _sz, C.c_uint,
+                                              C.c_uint64, _p]),
     "kb_gemm_splitk_partials_workspace_size": (_sz, [_i64, _i64, _i64]),
     "kb_gemm_splitk_partials_3xtf32": (_int, [_p, _p, _i64, _i64, _i64, _p, _sz, C.POINTER(C.c_int), _p]),
 }

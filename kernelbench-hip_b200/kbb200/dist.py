@@ -64,13 +64,29 @@ def shard(t: torch.Tensor, rank: int, world: int, dim: int = 0) -> torch.Tensor:
 # at 2 KiB and 30.7 vs 19.5 at 256 KiB (every rank's pushes grow with the
 # world size, NCCL's ring traffic does not).
 PEER_MAX_BYTES = 64
+# The fused sharded kernels (one CTA pushes this rank's fold to every peer at
+# the end of the partial pass) serve exchanges up to this size on any world
+# size: BatchNorm's 16 C + 8 bytes for C <= 1024.  The push is a few KiB per
+# peer from one CTA, so it does not grow into the standalone kernel's
+# per-rank traffic problem; larger exchanges keep the three-step form.
+FUSED_MAX_BYTES = 16 * 1024 + 8
 
 
 def peer_path(comm, nbytes: int) -> bool:
-    """Whether an exchange of nbytes per rank goes through the PeerComm.
-    Every rank passes the same nbytes and world size, so all ranks take the
-    same path and the collective order stays identical."""
-    return comm is not None and (comm.world <= 2 or nbytes <= PEER_MAX_BYTES)
+    """Whether an exchange of nbytes per rank goes through the PeerComm: never
+    beyond the communicator's slot (comm.payload_bytes), which NCCL handles
+    instead.  Every rank passes the same nbytes and world size, so all ranks
+    take the same path and the collective order stays identical."""
+    return (comm is not None and nbytes <= comm.payload_bytes
+            and (comm.world <= 2 or nbytes <= PEER_MAX_BYTES))
+
+
+def _fused(comm, nbytes: int) -> bool:
+    """Whether the sharded reduction runs as one fused launch (partial pass
+    and exchange in the same kernel, kbb200.p2p.PeerComm): on the peer path,
+    whose one-CTA exchange carries at most FUSED_MAX_BYTES per rank."""
+    return (comm is not None and getattr(comm, "fused", False) and nbytes <= FUSED_MAX_BYTES
+            and nbytes <= comm.payload_bytes)
 
 
 def _all_reduce_sum(t: torch.Tensor, group=None, comm=None) -> torch.Tensor:
@@ -96,6 +112,9 @@ def mse_loss(a: torch.Tensor, b: torch.Tensor, total_n: int | None = None, out=N
     result).  The element count travels with the partial sum, so shards may
     differ in size (or be empty); total_n overrides it."""
     k = kernels or _default_kernels()
+    if total_n is None and _fused(comm, 16):
+        y = out if out is not None else torch.empty((), device=a.device, dtype=torch.float32)
+        return comm.mse_loss(a, b, y)
     part = k.mse_partial(a, b)
     _all_reduce_sum(part, group, comm)
     return k.mse_finalize(part, total_n if total_n is not None else 0, out=out)
@@ -104,8 +123,11 @@ def mse_loss(a: torch.Tensor, b: torch.Tensor, total_n: int | None = None, out=N
 def frobenius_normalize(x: torch.Tensor, out=None, group=None, kernels=None, comm=None):
     """x_shard / ||x||_F where the norm spans all ranks' shards."""
     k = kernels or _default_kernels()
-    part = k.sumsq_partial(x)
-    _all_reduce_sum(part, group, comm)
+    if _fused(comm, 8):
+        part = comm.sumsq(x, torch.empty((), device=x.device, dtype=torch.float64))
+    else:
+        part = k.sumsq_partial(x)
+        _all_reduce_sum(part, group, comm)
     return k.scale_by_inv_norm(x, part, out=out)
 
 
@@ -119,8 +141,12 @@ def batch_norm_train(x: torch.Tensor, weight=None, bias=None, eps: float = 1e-5,
     empty slice still updates its running statistics.  total_count
     overrides the count."""
     k = kernels or _default_kernels()
-    stats = k.batch_norm_stats(x)
-    _all_reduce_sum(stats, group, comm)
+    nbytes = 8 * (2 * x.shape[1] + 1)
+    if _fused(comm, nbytes) and x.shape[1] > 0:
+        stats = comm.batch_norm_stats(x, torch.empty(2 * x.shape[1] + 1, device=x.device, dtype=torch.float64))
+    else:
+        stats = k.batch_norm_stats(x)
+        _all_reduce_sum(stats, group, comm)
     count = total_count if total_count is not None else 0
     return k.batch_norm_apply(x, stats, count, weight, bias, eps, momentum, running_mean,
                               running_var, out=out)

@@ -10,13 +10,20 @@ rank's buffer, raises a system-scope flag on each, waits for the peers' flags
 and sums the parts that arrived in rank order — identical bits on every rank.
 Plain peer loads and stores over NVLink: no multicast objects.
 
+For MSE, Frobenius and BatchNorm the exchange is fused into the kernel that
+computes the shard's partial (`mse_loss`, `sumsq`, `batch_norm_stats`): the
+CTA that finishes the partial pass last pushes the folded values to every
+peer and sums what arrived, so partial, all-reduce and finish are one
+launch.  Those calls reuse one zeroed workspace owned by the communicator.
+
 Every rank must make the same calls in the same order.  A wait that runs
-past `timeout_s` makes the kernel record a fault and skip its output;
-`check()` raises it, after which the communicator must be closed.
+past `timeout_s` makes the kernel record a fault and write NaN as its
+output; `check()` raises it, after which the communicator must be closed.
 """
 from __future__ import annotations
 
 import ctypes as C
+import math
 
 import torch
 import torch.distributed as tdist
@@ -25,8 +32,10 @@ from ._lib import LIB, KbError, check
 
 
 class PeerComm:
-    def __init__(self, group=None, payload_bytes: int = 1 << 20, timeout_s: float = 2.0, device=None):
+    def __init__(self, group=None, payload_bytes: int = 1 << 20, timeout_s: float = 2.0, device=None,
+                 fused: bool = True):
         self.group = group
+        self.fused = fused  # sharded MSE / Frobenius / BatchNorm as one launch each (kbb200.dist)
         self.rank = tdist.get_rank(group)
         self.world = tdist.get_world_size(group)
         self.device = torch.device(device) if device is not None else torch.device(
@@ -35,6 +44,7 @@ class PeerComm:
         self.buf_bytes = LIB.kb_p2p_buffer_bytes(self.payload_bytes, self.world)
         self.timeout_ns = int(timeout_s * 1e9)
         self.epoch = 0
+        self._ws = None
         self._own = C.c_void_p()
         self._opened: list[int] = []
         with torch.cuda.device(self.device):
@@ -59,7 +69,9 @@ class PeerComm:
         tdist.barrier(group=group)
 
     def _next(self) -> int:
-        self.epoch = self.epoch % 0xFFFFFFFF + 1  # 1, 2, ... (never 0: flags start zeroed)
+        # 1, 2, ..., 0xFFFFFFFE, 1, ...: never 0 (flags start zeroed), and an even
+        # period, so the slot (epoch & 1) still alternates across the wrap
+        self.epoch = self.epoch % 0xFFFFFFFE + 1
         return self.epoch
 
     def _stream(self, t: torch.Tensor) -> int:
@@ -87,6 +99,47 @@ class PeerComm:
                                                   partials.data_ptr(), int(splits), out.data_ptr(), n,
                                                   self._next(), self.timeout_ns, self._stream(out)))
         return out
+
+    # ---- fused sharded reductions: partial pass + exchange in one launch
+    def _workspace(self, nbytes: int) -> torch.Tensor:
+        """A zeroed workspace reused by every fused call (they run in stream
+        order; each leaves its arrival counter at zero)."""
+        if self._ws is None or self._ws.numel() < nbytes:
+            self._ws = torch.zeros(max(int(nbytes), 1 << 16), dtype=torch.uint8, device=self.device)
+        return self._ws
+
+    def _peer_args(self) -> tuple:
+        return (self.bufs.data_ptr(), self.rank, self.world, self.buf_bytes, self._next(), self.timeout_ns)
+
+    def mse_loss(self, a: torch.Tensor, b: torch.Tensor, out: torch.Tensor) -> torch.Tensor:
+        """out = mean over every rank's elements of (a - b)^2 (this rank: its
+        shard a, b), one launch (kb_mse_sharded_f32)."""
+        ws = self._workspace(LIB.kb_sharded_workspace_size())
+        check("kb_mse_sharded_f32", LIB.kb_mse_sharded_f32(a.data_ptr(), b.data_ptr(), out.data_ptr(), a.numel(),
+                                                            ws.data_ptr(), ws.numel(), *self._peer_args(),
+                                                            self._stream(a)))
+        return out
+
+    def sumsq(self, x: torch.Tensor, total: torch.Tensor) -> torch.Tensor:
+        """total (fp64, one element) = sum over every rank's shard of x^2, one
+        launch (kb_sumsq_sharded_f64)."""
+        ws = self._workspace(LIB.kb_sharded_workspace_size())
+        check("kb_sumsq_sharded_f64", LIB.kb_sumsq_sharded_f64(x.data_ptr(), total.data_ptr(), x.numel(),
+                                                                ws.data_ptr(), ws.numel(), *self._peer_args(),
+                                                                self._stream(x)))
+        return total
+
+    def batch_norm_stats(self, x: torch.Tensor, stats: torch.Tensor) -> torch.Tensor:
+        """stats (fp64, 2C + 1) = global per-channel sums, sums of squares and
+        elements per channel over every rank's batch shard, one launch
+        (kb_batchnorm_stats_sharded_f64)."""
+        N, Cc = x.shape[0], x.shape[1]
+        HW = math.prod(x.shape[2:])
+        ws = self._workspace(LIB.kb_batchnorm_sharded_workspace_size(N, Cc, HW))
+        check("kb_batchnorm_stats_sharded_f64",
+              LIB.kb_batchnorm_stats_sharded_f64(x.data_ptr(), stats.data_ptr(), N, Cc, HW, ws.data_ptr(),
+                                                 ws.numel(), *self._peer_args(), self._stream(x)))
+        return stats
 
     def check(self) -> None:
         """Synchronise and raise if a wait of this communicator's kernels expired."""

@@ -133,6 +133,94 @@ FAMILIES = {
     "structured": ["matmul_transposed_a", "matmul_symmetric", "diag_matmul", "matmul_small_k"],
     "adjacent": ["avg_pool2d", "cumsum", "cross_entropy"],
 }
+# the 19 operators of the benchmark configs, in config order
+FAMILIES["northstar"] = (FAMILIES["gelu"] + FAMILIES["rownorm"] + FAMILIES["reductions"]
+                         + FAMILIES["spatial"] + FAMILIES["gemm"])
+FAMILIES["all"] = FAMILIES["northstar"] + FAMILIES["structured"] + FAMILIES["adjacent"]
+
+# ---------------------------------------------------------------- sharding
+# How each op's global input is partitioned over the ranks of a multi-GPU
+# job: input name -> the dimension cut into contiguous shards
+# (kbb200.dist.shard_range; the first n % world ranks take one extra unit).
+# Inputs not named are replicated on every rank (the GEMM's B, the matvec's
+# x, affine parameters).  The output is cut along the same units.
+SHARD_DIMS: dict[str, dict[str, int]] = {
+    **{n: {"x": 0} for n in ("gelu_tanh", "gelu_erf", "swish", "relu", "layer_norm", "rms_norm",
+                             "softmax", "log_softmax", "sum_dim", "mean_dim", "argmax_dim",
+                             "frobenius_normalize", "max_pool2d", "batch_norm_train", "avg_pool2d",
+                             "cumsum")},
+    "mse_loss": {"predictions": 0, "targets": 0},
+    "cross_entropy": {"predictions": 0, "targets": 0},
+    "matmul": {"A": 0},                      # rows of A and C; B replicated
+    "matmul_symmetric": {"A": 0},
+    "matmul_small_k": {"A": 0},
+    "matmul_transposed_a": {"A": 1},         # A stored [K, M]: columns are C's rows
+    "bmm": {"A": 0, "B": 0},                 # batch
+    "matmul_splitk": {"A": 1, "B": 0},       # K slices; partial C summed across ranks
+    "gemv": {"A": 0},                        # rows of A and y; x replicated
+    "diag_matmul": {"A": 0, "B": 0},
+}
+# The cross-GPU step of the ops whose result spans every shard (one
+# collective between a local partial kernel and a local finish, kbb200.dist);
+# every other op needs none.
+EXCHANGE: dict[str, str] = {
+    "mse_loss": "all-reduce of fp64 (sum of squares, count): 16 B",
+    "frobenius_normalize": "all-reduce of the fp64 sum of squares: 8 B",
+    "batch_norm_train": "all-reduce of fp64 per-channel (sum, sum of squares) + count: 16 C + 8 B",
+    "matmul_splitk": "all-reduce of the fp32 partial C: 4 M N B",
+    "cross_entropy": "all-reduce of fp64 (sum of losses, rows): 16 B",
+}
+
+# Ops that read the very same input tensors as an earlier op of the step (same
+# shapes and distribution): the bench keeps one copy on the device and on the
+# host.  Each is >= 1 GB and read front to back, so at most the last 126 MB
+# of the earlier op's pass can still sit in L2 when the later op starts at
+# the front; it is evicted long before the later op gets there.
+SHARED_INPUTS = {"rms_norm": "layer_norm", "log_softmax": "softmax", "mean_dim": "sum_dim",
+                 "argmax_dim": "sum_dim"}
+
+
+def shard_shapes(w: Workload, rank: int, world: int) -> dict:
+    """Input shapes of rank's shard of workload `w` (all inputs, sharded or
+    replicated)."""
+    from .dist import shard_range
+
+    dims = SHARD_DIMS.get(w.name, {})
+    out = {}
+    for name, shape, _ in w.inputs:
+        shape = list(shape)
+        if name in dims and world > 1:
+            d = dims[name]
+            lo, hi = shard_range(shape[d], rank, world)
+            shape[d] = hi - lo
+        out[name] = tuple(shape)
+    return out
+
+
+def shard_fraction(w: Workload, rank: int, world: int) -> float:
+    """The share of the op's units (and algorithmic work) a rank holds."""
+    if world <= 1:
+        return 1.0
+    name, d = next(iter(SHARD_DIMS[w.name].items()))
+    full = dict((n, s) for n, s, _ in w.inputs)[name][d]
+    return shard_shapes(w, rank, world)[name][d] / full
+
+
+# ---------------------------------------------------------------- rooflines
+def roofline_seconds(w: Workload, hbm_gbs: float, tensor_tflops: float) -> float:
+    """Lower bound on one launch's time on one B200: the algorithmic bytes at
+    the measured copy bandwidth, and for tensor-core contractions also the
+    useful FLOPs at the 3xTF32 ceiling (the larger of the two)."""
+    t = w.algo_bytes / (hbm_gbs * 1e9)
+    if w.bound == "tensor":
+        t = max(t, w.flops / (tensor_tflops * 1e12))
+    return t
+
+
+def roofline_bound(w: Workload, hbm_gbs: float, tensor_tflops: float) -> str:
+    if w.bound == "tensor" and w.flops / (tensor_tflops * 1e12) >= w.algo_bytes / (hbm_gbs * 1e9):
+        return "tensor"
+    return "hbm"
 
 
 def fill_(t: torch.Tensor, dist: str, gen: torch.Generator, fan_in: int = 1) -> torch.Tensor:
@@ -159,19 +247,31 @@ def fill_(t: torch.Tensor, dist: str, gen: torch.Generator, fan_in: int = 1) -> 
     raise ValueError(dist)
 
 
-def make_inputs(w: Workload, device, seed: int = 0, shapes: dict | None = None) -> list[torch.Tensor]:
+def make_inputs(w: Workload, device, seed: int = 0, shapes: dict | None = None,
+                global_scale: bool = False) -> list[torch.Tensor]:
     """Seeded synthetic inputs for workload `w` generated directly on `device`
-    (device RNG; the parity tests use CPU-seeded inputs instead)."""
+    (device RNG; the parity tests use CPU-seeded inputs instead).  `shapes`
+    overrides input shapes (a reduced case, or a rank's shard).  The GEMM
+    operands' scale 1/sqrt(K) follows the K of the given shapes, or with
+    `global_scale` the workload's own K (a shard of a split-K job)."""
     gen = torch.Generator(device=device)
     gen.manual_seed(seed)
     out = []
-    for name, shape, dist in w.inputs:
-        shape = tuple((shapes or {}).get(name, shape))
+    for name, full, dist in w.inputs:
+        shape = tuple((shapes or {}).get(name, full))
         dtype = torch.int64 if dist == "labels" else torch.float32
-        t = torch.empty(shape, device=device, dtype=dtype)
         if dist == "labels":  # number of classes: the last dim of the first input
             fan_in = out[0].shape[-1]
+        elif dist == "gemm":  # K: A's last dim, B's second to last
+            ref = full if global_scale else shape
+            fan_in = ref[-2] if name == "B" else ref[-1]
         else:
-            fan_in = shape[-2] if (dist == "gemm" and name == "B") else (shape[-1] if dist == "gemm" else 1)
+            fan_in = 1
+        if dist == "gemm_sym" and shape[0] != shape[-1]:
+            # rows of a symmetric matrix: draw the whole square, keep the first rows
+            sq = fill_(torch.empty(full, device=device, dtype=dtype), dist, gen, fan_in)
+            out.append(sq[: shape[0]].contiguous())
+            continue
+        t = torch.empty(shape, device=device, dtype=dtype)
         out.append(fill_(t, dist, gen, fan_in))
     return out

@@ -158,8 +158,41 @@ def test_peer_path_routing():
 
     from kbb200.dist import PEER_MAX_BYTES, peer_path
 
-    two, four, eight = (SimpleNamespace(world=w) for w in (2, 4, 8))
+    two, four, eight = (SimpleNamespace(world=w, payload_bytes=1 << 20) for w in (2, 4, 8))
     assert peer_path(two, 8) and peer_path(two, 256 * 1024)
     assert peer_path(four, 16) and peer_path(eight, PEER_MAX_BYTES)
     assert not peer_path(four, PEER_MAX_BYTES + 1) and not peer_path(eight, 256 * 1024)
     assert not peer_path(None, 8)
+    # an exchange larger than the communicator's slot goes to NCCL, on any world size
+    small = SimpleNamespace(world=2, payload_bytes=4096)
+    assert peer_path(small, 4096) and not peer_path(small, 4097)
+
+
+def test_fused_routing():
+    """The fused one-launch sharded reductions serve exchanges up to
+    FUSED_MAX_BYTES on every world size, only with a PeerComm that has them
+    enabled and whose slot is large enough."""
+    from types import SimpleNamespace
+
+    from kbb200.dist import FUSED_MAX_BYTES, _fused
+
+    c8 = SimpleNamespace(world=8, payload_bytes=1 << 20, fused=True)
+    assert _fused(c8, 16) and _fused(c8, 8 * 257) and _fused(c8, FUSED_MAX_BYTES)
+    assert not _fused(c8, FUSED_MAX_BYTES + 1)
+    assert not _fused(SimpleNamespace(world=2, payload_bytes=1 << 20, fused=False), 16)
+    assert not _fused(SimpleNamespace(world=2, payload_bytes=1024, fused=True), 2056)
+    assert not _fused(None, 16)
+
+
+def test_peer_epoch_wrap_keeps_slots_alternating():
+    """PeerComm's epoch never takes 0 (the flags start zeroed) and keeps an
+    even period, so the slot (epoch & 1) of two consecutive calls differs,
+    across the 32-bit wrap too."""
+    from kbb200.p2p import PeerComm
+
+    comm = object.__new__(PeerComm)  # the counter alone: no process group, no buffers
+    comm.epoch = 0xFFFFFFFE - 3
+    seen = [comm._next() for _ in range(8)]
+    assert 0 not in seen and max(seen) <= 0xFFFFFFFE
+    assert all((a ^ b) & 1 for a, b in zip(seen, seen[1:])), seen
+    assert 1 in seen  # it wrapped

@@ -128,16 +128,151 @@ def _worker(rank, world, port, q):
 def test_sharded_ops_on_several_gpus(world):
     if torch.cuda.device_count() < world:
         pytest.skip(f"needs {world} GPUs")
+    _run_workers(_worker, world)
+
+
+# uneven batch splits of BatchNorm's 64 images (every rank non-empty)
+BN_SPLITS = {2: [37, 27], 4: [23, 9, 17, 15], 8: [13, 5, 8, 8, 9, 7, 6, 8]}
+
+
+def _bench_worker(rank, world, port, q):
+    """The sharded ops at the benchmark shapes: every rank draws the same
+    global input on its own GPU (seeded device generator), keeps its shard,
+    runs the sharded op and compares with an fp64 evaluation of the global op
+    on the device and with the single-GPU kernel on the whole input."""
+    try:
+        for p in (str(REPO), str(REPO / "kernelbench-hip_b200")):
+            if p not in sys.path:
+                sys.path.insert(0, p)
+        os.environ.update(MASTER_ADDR="127.0.0.1", MASTER_PORT=str(port), NCCL_NVLS_ENABLE="0")
+        torch.cuda.set_device(rank)
+        dev = torch.device("cuda", rank)
+        import torch.distributed as tdist
+        import torch.nn.functional as F
+
+        tdist.init_process_group("nccl", rank=rank, world_size=world, device_id=dev,
+                                 timeout=datetime.timedelta(seconds=120))
+        from kbb200 import dist, ops
+        from kbb200.p2p import PeerComm
+
+        comm = PeerComm(payload_bytes=1 << 20, timeout_s=10.0)
+        res = {}
+
+        def gen(seed):
+            return torch.Generator(device=dev).manual_seed(seed)
+
+        try:
+            # MSE over two 2^28 vectors, contiguous slices
+            n = 1 << 28
+            a = torch.randn(n, device=dev, generator=gen(1))
+            b = torch.randn(n, device=dev, generator=gen(2))
+            want = float(((a.double() - b.double()) ** 2).mean())
+            sa, sb = dist.shard(a, rank, world), dist.shard(b, rank, world)
+            for label, c in (("nccl", None), ("p2p", comm)):
+                got = float(dist.mse_loss(sa, sb, comm=c))
+                res[f"mse_2^28_{label}"] = (got, want, 1e-3)
+            res["mse_2^28_single_gpu"] = (float(ops.mse_loss(a, b)), want, 1e-3)
+            del a, b, sa, sb
+
+            # Frobenius normalisation of [256, 1024, 1024], batch shards
+            x = torch.randn(256, 1024, 1024, device=dev, generator=gen(3))
+            lo, hi = dist.shard_range(256, rank, world)
+            norm = float(torch.linalg.vector_norm(x.double()))
+            for label, c in (("nccl", None), ("p2p", comm)):
+                y = dist.frobenius_normalize(x[lo:hi], comm=c)
+                ref = (x[lo:hi].double() / norm).float()
+                rel = float(((y - ref).abs() / (ref.abs() + 1e-12)).max())
+                res[f"frobenius_max_rel_err_{label}"] = (rel, 0.0, 1e-5)
+            del x, y, ref
+
+            # BatchNorm [64, 128, 256, 256], uneven batch shards, running statistics
+            x = torch.randn(64, 128, 256, 256, device=dev, generator=gen(4)) * 1.5 + 0.25
+            w = 1 + 0.02 * torch.randn(128, device=dev, generator=gen(5))
+            bb = 0.02 * torch.randn(128, device=dev, generator=gen(6))
+            sizes = BN_SPLITS[world]
+            lo = sum(sizes[:rank])
+            hi = lo + sizes[rank]
+            rm64, rv64 = torch.zeros(128, device=dev, dtype=torch.float64), torch.ones(128, device=dev,
+                                                                                       dtype=torch.float64)
+            ref = F.batch_norm(x.double(), rm64, rv64, w.double(), bb.double(),
+                               training=True, momentum=0.1, eps=1e-5)[lo:hi].float()
+            for label, c in (("nccl", None), ("p2p", comm)):
+                rm, rv = torch.zeros(128, device=dev), torch.ones(128, device=dev)
+                y = dist.batch_norm_train(x[lo:hi], w, bb, 1e-5, 0.1, rm, rv, comm=c)
+                res[f"batchnorm_max_err_{label}"] = (float((y - ref).abs().max()), 0.0, 1e-5)
+                res[f"batchnorm_running_mean_{label}"] = (rm.cpu().numpy(), rm64.float().cpu().numpy(), 1e-5)
+                res[f"batchnorm_running_var_{label}"] = (rv.cpu().numpy(), rv64.float().cpu().numpy(), 1e-5)
+            del x, y, ref
+
+            # split-K 256 x 4,194,304 @ 4,194,304 x 256, K slices
+            K = 4194304
+            A = torch.randn(256, K, device=dev, generator=gen(7)) / K ** 0.5
+            B = torch.randn(K, 256, device=dev, generator=gen(8)) / K ** 0.5
+            want = torch.zeros(256, 256, device=dev, dtype=torch.float64)
+            for k0 in range(0, K, 1 << 19):  # fp64 in chunks of K (bounded memory)
+                want += A[:, k0:k0 + (1 << 19)].double() @ B[k0:k0 + (1 << 19)].double()
+            lo, hi = dist.shard_range(K, rank, world)
+            As, Bs = A[:, lo:hi].contiguous(), B[lo:hi]
+            del A, B
+            outs = {}
+            for label, c in (("nccl", None), ("p2p", comm)):
+                cmat = dist.matmul_splitk(As, Bs, comm=c)
+                outs[label] = cmat
+                err = float(((cmat.double() - want).abs() - 1e-3 * want.abs()).max())
+                res[f"splitk_K4M_excess_err_{label}"] = (max(err, 0.0), 0.0, 1e-3)
+            again = dist.matmul_splitk(As, Bs, comm=comm)
+            res["splitk_K4M_p2p_deterministic"] = (float(torch.equal(again, outs["p2p"])), 1.0, 0.0)
+            gathered = [torch.empty_like(again) for _ in range(world)]
+            tdist.all_gather(gathered, again)
+            res["splitk_K4M_replicated"] = (float(all(torch.equal(gathered[0], t) for t in gathered)), 1.0, 0.0)
+            del As, Bs
+
+            # row shards without an exchange: SGEMM rows of 8192^3, matvec rows
+            A = torch.randn(8192, 8192, device=dev, generator=gen(9)) / 8192 ** 0.5
+            B = torch.randn(8192, 8192, device=dev, generator=gen(10)) / 8192 ** 0.5
+            lo, hi = dist.shard_range(8192, rank, world)
+            whole = ops.matmul(A, B)
+            res["sgemm_rows_equal_whole"] = (float(torch.equal(ops.matmul(A[lo:hi], B), whole[lo:hi])), 1.0, 0.0)
+            del A, B, whole
+            A = torch.randn(4096, 1 << 20, device=dev, generator=gen(11))
+            v = torch.randn(1 << 20, device=dev, generator=gen(12))
+            lo, hi = dist.shard_range(4096, rank, world)
+            ref = (A[lo:hi].double() @ v.double()).float()
+            y = ops.gemv(A[lo:hi], v)
+            res["gemv_rows_max_rel_err"] = (float(((y - ref).abs() / (1e-3 + ref.abs())).max()), 0.0, 1e-3)
+            del A, v
+            comm.check()
+        finally:
+            comm.close()
+        torch.cuda.synchronize()
+        tdist.destroy_process_group()
+        q.put((rank, "ok", res))
+    except Exception as e:
+        q.put((rank, "err", f"{type(e).__name__}: {e}\n{traceback.format_exc()[-800:]}"))
+
+
+@pytest.mark.parametrize("world", [2, 4, 8])
+def test_sharded_ops_at_benchmark_shapes(world):
+    """MSE on 2^28 elements, Frobenius [256, 1024, 1024], BatchNorm
+    [64, 128, 256, 256] split unevenly by batch, split-K with K = 4,194,304
+    split by K, and the row-sharded SGEMM / matvec, each over NCCL and over
+    the peer all-reduce, against the global op."""
+    if torch.cuda.device_count() < world:
+        pytest.skip(f"needs {world} GPUs")
+    _run_workers(_bench_worker, world, timeout=600)
+
+
+def _run_workers(target, world, timeout=300):
     ctx = mp.get_context("spawn")
     q = ctx.Queue()
     port = _free_port()
-    procs = [ctx.Process(target=_worker, args=(r, world, port, q)) for r in range(world)]
+    procs = [ctx.Process(target=target, args=(r, world, port, q)) for r in range(world)]
     for p in procs:
         p.start()
     out = {}
     try:
         for _ in range(world):
-            rank, status, res = q.get(timeout=300)
+            rank, status, res = q.get(timeout=timeout)
             out[rank] = (status, res)
     finally:
         for p in procs:

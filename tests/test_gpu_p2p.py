@@ -6,7 +6,7 @@ peer would push into our buffer and its ready flag in our header are written
 by the host before the launch, so no kernel waits for another kernel.  Checked: the rank-ordered sum
 (float32, float64, in place), the fused split-K form, slot alternation over
 epochs, and a wait that runs out (a peer flag that nothing sets) — the
-kernel reports it in the fault word and leaves dst untouched.  The real
+kernel reports it in the fault word and fills dst with NaN.  The real
 multi-GPU path is in tests/test_gpu_dist.py.
 """
 from __future__ import annotations
@@ -123,7 +123,8 @@ def test_splitk_fused_reduction(cuda_device):
 
 def test_peer_that_never_signals_times_out_and_reports(cuda_device):
     """A flag that nothing sets: the bounded wait expires (50 ms), the fault
-    word names phase 2 (peer signal) and rank 1, and dst is not written."""
+    word names phase 2 (peer signal) and rank 1, and dst holds NaN, so an
+    in-place exchange that failed cannot pass for this rank's partial."""
     em = Emulated(cuda_device)
     try:
         mine = torch.randn(64, dtype=torch.float64, device=cuda_device)
@@ -132,7 +133,7 @@ def test_peer_that_never_signals_times_out_and_reports(cuda_device):
                                                           mine.data_ptr(), out.data_ptr(), 64, 1, 50_000_000,
                                                           _stream()))
         assert _fault() == (2 << 8) | 1
-        assert torch.equal(out, torch.full_like(mine, 7.0))
+        assert bool(torch.isnan(out).all())
         # the device is still usable afterwards
         assert float((mine * 2).sum()) == pytest.approx(float(mine.sum()) * 2)
     finally:

@@ -5,8 +5,8 @@ memory themselves (a host framework owns all device allocations, or the call
 sits in a latency-bound loop where cudaMalloc's implicit synchronisation is
 not allowed): its scratch is a fixed 128 KiB device array inside the library
 instead of caller workspace.  These tests call it through the C ABI and check
-it against the workspace entry point, kb_batchnorm_train_f32, on two calls in
-a row (the second with a different shape, so leftovers of the first call in
+it against the workspace entry point, kb_batchnorm_train_f32, and the fp64
+oracle, on two calls in a row (the second with a different shape, so leftovers of the first call in
 the shared array cannot leak into the result), plus the size limit.
 
 This file is collected last (test_zz_*) so that a failing run that stops at
@@ -14,8 +14,7 @@ the first failure has already run every other test.
 """
 from __future__ import annotations
 
-import ctypes as C
-
+import numpy as np
 import pytest
 import torch
 
@@ -38,6 +37,7 @@ def _call_noalloc(x, w, b, y, rm, rv, eps=1e-5, momentum=0.1):
 @pytest.mark.parametrize("shapes", [[(8, 64, 32, 32), (3, 200, 17, 19)]])
 def test_noalloc_matches_workspace_entry(shapes, cuda_device):
     from kbb200 import ops
+    from oracle import ops as O
 
     for shape in shapes:  # two calls in a row, different shapes
         g = torch.Generator(device=cuda_device).manual_seed(sum(shape))
@@ -54,6 +54,12 @@ def test_noalloc_matches_workspace_entry(shapes, cuda_device):
         torch.testing.assert_close(y, ref, atol=TOL, rtol=TOL)
         torch.testing.assert_close(rm, rm_ref, atol=TOL, rtol=TOL)
         torch.testing.assert_close(rv, rv_ref, atol=TOL, rtol=TOL)
+        # and directly against the fp64 oracle, not only the workspace entry
+        xh, wh, bh = x.cpu().numpy(), w.cpu().numpy(), b.cpu().numpy()
+        np.testing.assert_allclose(y.cpu().numpy(), O.batch_norm_train(xh, wh, bh), atol=TOL, rtol=TOL)
+        erm, erv = O.batch_norm_running_update(xh, np.zeros(Cc), np.ones(Cc))
+        np.testing.assert_allclose(rm.cpu().numpy(), erm, atol=TOL, rtol=TOL)
+        np.testing.assert_allclose(rv.cpu().numpy(), erv, atol=TOL, rtol=TOL)
 
 
 def test_noalloc_rejects_more_channels_than_its_scratch(cuda_device):
