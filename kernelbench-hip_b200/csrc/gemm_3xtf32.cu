@@ -950,10 +950,72 @@ int splitk_count(int64_t M, int64_t N, int64_t K, int sms) {
   return (int)sp;
 }
 
+// K splits for a plain GEMM whose tiles fill the persistent grid badly.
+// The CTAs walk the tiles in waves of `sms`; a GEMM with 1.73 waves of
+// tiles (a 1024 x 8192 row shard of 8192^3 on 8 GPUs: 256 tiles on 148
+// SMs) pays for 2 full waves.  Cutting K into s splits gives s x tiles
+// shorter work units that fill the waves more evenly; it costs one partial
+// tile per split in memory, a deterministic reduction pass (s + 1 reads and
+// writes of C's size) and a per-unit pipeline fill.  Model, per SM: a 16-deep
+// K block takes t_kb (0.68 us measured at 8192^3 in steady state), a work
+// unit t_unit more; the reduction runs at HBM speed.  The split is taken when
+// the model saves at least 3 %.
+int wave_splits(int64_t M, int64_t N, int64_t K, int sms) {
+  constexpr double t_kb = 0.68e-6, t_unit = 2.0e-6, t_launch = 5.0e-6, hbm = 6.4e12;
+  const int64_t tiles = ceil_div(M, BM) * ceil_div(N, N > 128 ? 256 : 128);
+  const int64_t nk = ceil_div(K, BK);
+  auto model = [&](int sp) {
+    const int64_t kbps = ceil_div(nk, sp);
+    const int64_t units = tiles * ceil_div(nk, kbps);
+    double t = (double)ceil_div(units, (int64_t)sms) * ((double)kbps * t_kb + t_unit);
+    if (sp > 1) t += (double)(sp + 1) * (double)M * (double)N * 4.0 / hbm + t_launch;
+    return t;
+  };
+  int best = 1;
+  double best_t = model(1);
+  for (int sp = 2; sp <= 8; ++sp) {
+    if (nk / sp < 8) break;  // at least 8 K blocks (128 of K) per split
+    const double t = model(sp);
+    if (t < best_t * 0.97) {
+      best = sp;
+      best_t = t;
+    }
+  }
+  return best;
+}
+
 }  // namespace gemm
 }  // namespace kb
 
 extern "C" {
+
+size_t kb_sgemm_workspace_size(int64_t M, int64_t N, int64_t K, int trans_a) {
+  if (M <= 0 || N <= 0 || K <= 0 || trans_a) return 0;
+  const int sp = kb::gemm::wave_splits(M, N, K, kb::sm_count());
+  return sp > 1 ? (size_t)sp * M * N * sizeof(float) : 0;
+}
+
+int kb_sgemm_3xtf32_ws(const float* A, const float* B, float* C, int64_t M, int64_t N, int64_t K, int64_t lda,
+                       int64_t ldb, int64_t ldc, int trans_a, void* workspace, size_t workspace_bytes,
+                       kbStream stream) {
+  const char* name = "kb_sgemm_3xtf32_ws";
+  KB_REQUIRE(M >= 0 && N >= 0 && K >= 0, KB_ERR_INVALID_ARG, "%s: negative size", name);
+  if (M == 0 || N == 0) return KB_OK;
+  KB_REQUIRE(A && B && C, KB_ERR_INVALID_ARG, "%s: null pointer", name);
+  KB_REQUIRE(lda >= (trans_a ? M : K) && ldb >= N && ldc >= N, KB_ERR_INVALID_ARG,
+             "%s: leading dimension too small", name);
+  kb::gemm::GemmArgs g{A, B, C, 1, M, N, K, lda, ldb, ldc, 0, 0, 0, trans_a != 0};
+  g.sA = lda * (trans_a ? K : M);
+  g.sB = ldb * K;
+  g.sC = ldc * M;
+  int sp = trans_a ? 1 : kb::gemm::wave_splits(M, N, K, kb::sm_count());
+  // a workspace too small for the split (or misaligned, or an operand layout
+  // the TMA path cannot describe) runs the GEMM unsplit: same result class
+  if (sp > 1 && (!workspace || workspace_bytes < (size_t)sp * M * N * sizeof(float) ||
+                 !kb::aligned16(workspace) || !kb::gemm::tma_ok(g)))
+    sp = 1;
+  return kb::gemm::run_gemm(g, sp, static_cast<float*>(workspace), stream);
+}
 
 int kb_read_fault(int clear, int* value) {
   KB_REQUIRE(value, KB_ERR_INVALID_ARG, "kb_read_fault: null pointer");

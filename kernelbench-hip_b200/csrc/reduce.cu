@@ -260,14 +260,16 @@ int make_peer(const char* name, void* const* bufs, int rank, int world, size_t b
 // the per-CTA partials
 constexpr size_t kShardedWorkspace = kShardedCounterBytes + kMaxPartials * sizeof(double);
 
-int launch_sharded(const char* name, const float* a, const float* b, int64_t n, void* ws, size_t ws_bytes,
-                   const PeerCtx& peer, float* out_f, double* out_d, cudaStream_t s) {
+// diff: MSE of (a, b); otherwise the sum of squares of a.  Explicit, because
+// an empty shard may come with null data pointers.
+int launch_sharded(const char* name, bool diff, const float* a, const float* b, int64_t n, void* ws,
+                   size_t ws_bytes, const PeerCtx& peer, float* out_f, double* out_d, cudaStream_t s) {
   if (int st = check_ws(name, ws, ws_bytes, kShardedWorkspace)) return st;
   unsigned* counter = static_cast<unsigned*>(ws);
   double* parts = reinterpret_cast<double*>(static_cast<char*>(ws) + kShardedCounterBytes);
   const bool vec = n > 0 && aligned16(a) && (!b || aligned16(b));
   const int grid = n > 0 ? reduce_grid(vec ? n / 4 : n) : 1;
-  if (b) sq_sharded_kernel<true><<<grid, kThreads, 0, s>>>(a, b, n, vec, parts, counter, peer, out_f, out_d);
+  if (diff) sq_sharded_kernel<true><<<grid, kThreads, 0, s>>>(a, b, n, vec, parts, counter, peer, out_f, out_d);
   else sq_sharded_kernel<false><<<grid, kThreads, 0, s>>>(a, nullptr, n, vec, parts, counter, peer, out_f, out_d);
   return check_launch(name);
 }
@@ -288,7 +290,7 @@ int kb_mse_sharded_f32(const float* a, const float* b, float* out, int64_t n, vo
   kb::PeerCtx peer;
   if (int st = kb::make_peer(name, bufs, rank, world, buf_bytes, epoch, timeout_ns, 2 * sizeof(double), &peer))
     return st;
-  return kb::launch_sharded(name, a, b, n, workspace, workspace_bytes, peer, out, nullptr, stream);
+  return kb::launch_sharded(name, true, a, b, n, workspace, workspace_bytes, peer, out, nullptr, stream);
 }
 
 int kb_sumsq_sharded_f64(const float* x, double* total, int64_t n, void* workspace, size_t workspace_bytes,
@@ -300,7 +302,7 @@ int kb_sumsq_sharded_f64(const float* x, double* total, int64_t n, void* workspa
   kb::PeerCtx peer;
   if (int st = kb::make_peer(name, bufs, rank, world, buf_bytes, epoch, timeout_ns, sizeof(double), &peer))
     return st;
-  return kb::launch_sharded(name, x, nullptr, n, workspace, workspace_bytes, peer, nullptr, total, stream);
+  return kb::launch_sharded(name, false, x, nullptr, n, workspace, workspace_bytes, peer, nullptr, total, stream);
 }
 
 size_t kb_mse_workspace_size(int64_t) { return kb::kMaxPartials * sizeof(double); }

@@ -54,6 +54,8 @@ SIGNATURES: dict[str, tuple] = {
     "kb_batchnorm_stats_f64": (_int, [_p, _p, _i64, _i64, _i64, _p, _sz, _p]),
     "kb_batchnorm_apply_f32": (_int, [_p, _p, _p, _p, _p, _i64, _i64, _i64, _i64, _float, _float, _p, _p, _p]),
     "kb_sgemm_3xtf32": (_int, [_p, _p, _p, _i64, _i64, _i64, _i64, _i64, _i64, _int, _p]),
+    "kb_sgemm_workspace_size": (_sz, [_i64, _i64, _i64, _int]),
+    "kb_sgemm_3xtf32_ws": (_int, [_p, _p, _p, _i64, _i64, _i64, _i64, _i64, _i64, _int, _p, _sz, _p]),
     "kb_bgemm_3xtf32": (_int, [_p, _p, _p, _i64, _i64, _i64, _i64, _p]),
     "kb_gemm_splitk_workspace_size": (_sz, [_i64, _i64, _i64]),
     "kb_gemm_splitk_3xtf32": (_int, [_p, _p, _p, _i64, _i64, _i64, _p, _sz, _p]),

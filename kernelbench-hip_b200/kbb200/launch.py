@@ -4,15 +4,17 @@ driver (scripts/run_batch.py:24-47) and its crash-safe baseline sweep
 (scripts/run_baselines.py:24-29, :62-63).
 
     python -m kbb200.launch --kind bench --ops northstar --gpus 1,2,4,8 --out sweep.json
+    python -m kbb200.launch --kind bench --ops northstar --split-family --gpus 1,8 --out per_op.json
     python -m kbb200.launch --kind eval --ops 40_LayerNorm,23_Softmax --gpus 1 --out evals.json
     python -m kbb200.launch --kind reference --ops northstar --out cpu.json
 
 Cell kinds (each cell is one command, run under `torch.distributed.run` with
 one process per GPU when it has more than one GPU):
-  bench      bench.py --workload <op> --gpus N: the op's global problem
-             sharded over N ranks; the cell records the max-over-ranks step
-             time, the op's roofline fraction and the parallel efficiency
-             T1 / (N * TN) against the same op's 1-GPU cell;
+  bench      bench.py --workload <op or family> --gpus N: the global
+             problem sharded over N ranks; the cell records the max-over-ranks
+             step time, per-op times and roofline fractions, and the parallel
+             efficiency T1 / (N * TN) against the 1-GPU cell (for a family
+             cell also per op);
   eval       the strict eval (tests/eval_b200.py) of one problem: parity on
              every rank, the reference's timing protocol, milestones;
   reference  bench.py --impl reference --workload <op>: the torch-eager fp32
@@ -168,14 +170,19 @@ def verdict(kind: str, op: str, ngpu: int, run: dict, timeout_s: float, out_file
 
 
 def add_efficiency(results: dict) -> None:
-    """parallel_eff = T1 / (N * TN) for every bench cell whose op has a
-    1-GPU cell."""
+    """parallel_eff = T1 / (N * TN) for every bench cell whose op (or family)
+    has a 1-GPU cell, and per op inside a family cell (from its per_op
+    times)."""
     for key, rec in results.items():
         if rec.get("kind") != "bench" or rec.get("milestone", -1) < 0:
             continue
         one = results.get(f"{rec['op']}@1gpu")
         if one and one.get("milestone", -1) >= 0 and rec.get("ms_per_step"):
             rec["parallel_eff"] = round(one["ms_per_step"] / (rec["ngpu"] * rec["ms_per_step"]), 4)
+            per1, perN = one.get("per_op") or {}, rec.get("per_op") or {}
+            if len(perN) > 1:
+                rec["per_op_parallel_eff"] = {n: round(per1[n]["ms"] / (rec["ngpu"] * d["ms"]), 4)
+                                              for n, d in perN.items() if n in per1 and d.get("ms")}
 
 
 def save(path: Path, results: dict) -> None:
@@ -237,15 +244,17 @@ def main(argv=None) -> int:
     ap.add_argument("--warmup", type=int, default=5)
     ap.add_argument("--redo", action="store_true", help="ignore recorded cells")
     ap.add_argument("--log-dir", default=None)
+    ap.add_argument("--split-family", action="store_true",
+                    help="one cell per op of a family (default: the family's ops share one bench step per cell)")
     a = ap.parse_args(argv)
     from .workloads import FAMILIES, WORKLOADS
 
-    if a.ops in FAMILIES:
+    if a.ops in FAMILIES and (a.kind == "eval" or a.split_family):
         ops = FAMILIES[a.ops]
         if a.kind == "eval":
             ops = [WORKLOADS[o].problem for o in ops]
     else:
-        ops = a.ops.split(",")
+        ops = a.ops.split(",")  # a family name stays one cell: all its ops in one bench step
     gpus = [1] if a.kind == "reference" else [int(g) for g in a.gpus.split(",")]
     log_dir = Path(a.log_dir) if a.log_dir else None
     if log_dir:

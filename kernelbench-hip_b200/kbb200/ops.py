@@ -382,6 +382,14 @@ def matmul(A, B, trans_a: bool = False, out=None):
         raise RuntimeError(f"{fn}: inner dimensions differ ({K} vs {B.shape[0]})")
     N = B.shape[1]
     y = _out_like(A, out, fn, (M, N))
+    ws_bytes = LIB.kb_sgemm_workspace_size(M, N, K, 1 if trans_a else 0)
+    if ws_bytes:  # K split into partial tiles for a better-filled grid (deterministic sum)
+        fn = "kb_sgemm_3xtf32_ws"
+        ws = _workspace(A, ws_bytes)
+        check(fn, LIB.kb_sgemm_3xtf32_ws(A.data_ptr(), B.data_ptr(), y.data_ptr(), M, N, K, A.stride(0),
+                                         B.stride(0), N, 1 if trans_a else 0, ws.data_ptr(), ws.numel(),
+                                         _stream(A)))
+        return y
     check(fn, LIB.kb_sgemm_3xtf32(A.data_ptr(), B.data_ptr(), y.data_ptr(), M, N, K, A.stride(0),
                                   B.stride(0), N, 1 if trans_a else 0, _stream(A)))
     return y

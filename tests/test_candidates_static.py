@@ -10,14 +10,21 @@
 from __future__ import annotations
 
 import importlib.util
+import os
+import sys
 from pathlib import Path
 
 import pytest
+import torch
 
 from oracle import problems
 from tests.protocol import build_candidate, candidate_entry, candidate_path, static_check
 
-REF_ANTIHACK = Path("/root/reference/harness/antihack.py")
+# a checkout of the reference (read-only); the tests that run its own harness
+# code skip where there is none
+REF_ROOT = Path(os.environ.get("KBB200_REFERENCE_DIR", "/root/reference"))
+REF_ANTIHACK = REF_ROOT / "harness" / "antihack.py"
+REF_EVAL = REF_ROOT / "harness" / "eval_protected.py"
 
 
 @pytest.mark.parametrize("name", problems.SUBSET)
@@ -43,6 +50,39 @@ def test_reference_antihack_accepts_candidate(name):
     src = candidate_path(name).read_text()
     res = mod.static_check(src, candidate_entry(src))
     assert res["ok"], res["violations"]
+
+
+@pytest.fixture(scope="module")
+def reference_eval():
+    """The reference's protected eval module, unmodified (its import pulls in
+    its own antihack and problems modules from the same directory)."""
+    if not REF_EVAL.exists():
+        pytest.skip("reference checkout not present")
+    saved = list(sys.path)
+    spec = importlib.util.spec_from_file_location("_ref_eval_protected", REF_EVAL)
+    mod = importlib.util.module_from_spec(spec)
+    try:
+        spec.loader.exec_module(mod)
+    finally:
+        sys.path[:] = saved
+    return mod
+
+
+@pytest.mark.parametrize("name", problems.SUBSET)
+def test_reference_eval_builds_candidate(name, reference_eval):
+    """The reference eval's own candidate handling (harness/eval_protected.py:
+    _candidate_entry :259-263, antihack.static_check :150-159, build_candidate
+    :286-300 with its restricted globals) accepts every candidate, and the
+    Model it returns constructs from the problem's init inputs.  The timed
+    GPU part of evaluate() pins cuda:0 and is not run here (no GPU)."""
+    src = candidate_path(name).read_text()
+    entry = reference_eval._candidate_entry(src)
+    assert entry and entry == candidate_entry(src)
+    assert reference_eval.antihack.static_check(src, entry)["ok"]
+    Model, e2 = reference_eval.build_candidate(src)
+    assert e2 == entry
+    _, _, get_init_inputs, _ = problems.load_problem(name)
+    assert isinstance(Model(*get_init_inputs()), torch.nn.Module)
 
 
 def test_static_check_catches_fallbacks():

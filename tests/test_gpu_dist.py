@@ -237,9 +237,15 @@ def _bench_worker(rank, world, port, q):
             A = torch.randn(4096, 1 << 20, device=dev, generator=gen(11))
             v = torch.randn(1 << 20, device=dev, generator=gen(12))
             lo, hi = dist.shard_range(4096, rank, world)
-            ref = (A[lo:hi].double() @ v.double()).float()
             y = ops.gemv(A[lo:hi], v)
-            res["gemv_rows_max_rel_err"] = (float(((y - ref).abs() / (1e-3 + ref.abs())).max()), 0.0, 1e-3)
+            # rows are independent with a fixed summation order: the shard's
+            # rows equal the whole-input kernel's bit for bit (that kernel is
+            # checked against torch at this shape by the parity tests); and
+            # against fp64, within fp32 accumulation error of 2^20-term rows
+            res["gemv_rows_equal_whole"] = (float(torch.equal(y, ops.gemv(A, v)[lo:hi])), 1.0, 0.0)
+            ref = A[lo:hi].double() @ v.double()
+            res["gemv_rows_fp64_excess"] = (float(((y.double() - ref).abs() - (1e-2 + 1e-3 * ref.abs())).clamp_min(0).max()),
+                                            0.0, 0.0)
             del A, v
             comm.check()
         finally:

@@ -366,6 +366,41 @@ def test_gemm_b_resident_small_k(shape, cuda_device):
     assert read_fault() == 0
 
 
+@pytest.mark.parametrize("mnk", [(1024, 8192, 8192), (256, 8192, 8192), (2048, 4096, 1024), (300, 520, 4096)])
+def test_sgemm_wave_split(mnk, cuda_device):
+    """Shapes whose tiles fill the persistent grid's waves badly take the K
+    split (kb_sgemm_3xtf32_ws; the first is one row shard of the 8192^3 GEMM
+    on 8 GPUs): fp32-level error, deterministic, and close to the unsplit
+    entry on the same operands."""
+    import ctypes as C
+
+    from kbb200 import ops as K
+    from kbb200._lib import LIB, check, read_fault
+
+    M, N, Kd = mnk
+    g = torch.Generator(device=cuda_device).manual_seed(M + Kd)
+    A = torch.randn(M, Kd, device=cuda_device, generator=g) / Kd ** 0.5
+    B = torch.randn(Kd, N, device=cuda_device, generator=g)
+    ws = LIB.kb_sgemm_workspace_size(M, N, Kd, 0)
+    if mnk[0] in (1024, 256):
+        assert ws > 0, "the row shard of 8192^3 should take the split"
+    got = K.matmul(A, B)
+    _gemm_check(got, A, B, f"wave split {mnk}")
+    assert torch.equal(got, K.matmul(A, B)), "must be deterministic"
+    plain = torch.empty_like(got)
+    check("kb_sgemm_3xtf32", LIB.kb_sgemm_3xtf32(A.data_ptr(), B.data_ptr(), plain.data_ptr(), M, N, Kd, Kd, N, N, 0,
+                                                torch.cuda.current_stream().cuda_stream))
+    torch.testing.assert_close(got, plain, atol=1e-5, rtol=1e-5)
+    # a workspace smaller than the split needs: the GEMM runs unsplit, same bits as the plain entry
+    small = torch.empty(16, dtype=torch.uint8, device=cuda_device)
+    out = torch.empty_like(got)
+    check("kb_sgemm_3xtf32_ws", LIB.kb_sgemm_3xtf32_ws(A.data_ptr(), B.data_ptr(), out.data_ptr(), M, N, Kd, Kd, N,
+                                                      N, 0, small.data_ptr(), 16,
+                                                      torch.cuda.current_stream().cuda_stream))
+    assert torch.equal(out, plain)
+    assert read_fault() == 0
+
+
 @pytest.mark.parametrize("mnk", [(512, 384, 256), (130, 260, 68), (4096, 2048, 136)])
 def test_sgemm_transposed_a(mnk, cuda_device):
     from kbb200 import ops as K

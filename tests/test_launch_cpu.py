@@ -97,3 +97,21 @@ def test_cell_commands_use_torchrun_beyond_one_gpu(tmp_path):
     assert str(tmp_path / "o.json") in ev and ev[-4] == "--problem"
     ref = cell_command("reference", "layer_norm", 1, 3, 1, tmp_path / "o.json")
     assert "--impl" in ref and ref[ref.index("--impl") + 1] == "reference"
+
+
+def test_family_cell_efficiency_per_op():
+    """A family cell (all ops in one bench step) gets the step's and every
+    op's parallel efficiency against the 1-GPU cell."""
+    from kbb200.launch import add_efficiency
+
+    res = {
+        "northstar@1gpu": {"kind": "bench", "op": "northstar", "ngpu": 1, "milestone": 1, "ms_per_step": 20.0,
+                           "per_op": {"matmul": {"ms": 5.0}, "mse_loss": {"ms": 0.32}}},
+        "northstar@8gpu": {"kind": "bench", "op": "northstar", "ngpu": 8, "milestone": 1, "ms_per_step": 2.7,
+                           "per_op": {"matmul": {"ms": 0.7}, "mse_loss": {"ms": 0.05}}},
+    }
+    add_efficiency(res)
+    r = res["northstar@8gpu"]
+    assert r["parallel_eff"] == pytest.approx(20.0 / (8 * 2.7), abs=1e-4)
+    assert r["per_op_parallel_eff"]["matmul"] == pytest.approx(5.0 / 5.6, abs=1e-4)
+    assert r["per_op_parallel_eff"]["mse_loss"] == pytest.approx(0.8, abs=1e-4)
