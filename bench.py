@@ -117,6 +117,8 @@ NCU_DRAM_BYTES: dict[str, float | None] = {
     "max_pool2d": 4.0 * (540.104192e6 + 107.429888e6),
     "gemv": 4.0 * (4299.227e6 + 3.568896e6),
     "batch_norm_train": 4.0 * (536.913408e6 + 4.80512e6 + 536.905984e6 + 490.593024e6),
+    # one full 8192^3 launch (grouped tile walk), profiles/gemm3x_8192cube_splitk.md
+    "matmul": 2278.3488e6 + 258.073344e6,
 }
 # write-back still in L2 at the end of a quarter-size capture, per capture:
 # output bytes per capture - captured DRAM writes (added back once)

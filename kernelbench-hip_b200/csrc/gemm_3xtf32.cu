@@ -301,6 +301,7 @@ struct Params {
   int run, runs;     // B-resident form: m-tiles per run, runs in all (tiles_z x tiles_n x segments);
                      // streaming form (run 0): tiles blockIdx.x + i * gridDim.x, n fastest
   int segs;          // B-resident form: runs per tile column
+  int group;         // streaming form: m-tiles per tile group (1: row-band order)
 };
 
 // One output tile: its corner, batch / split index and k-block range.
@@ -324,10 +325,21 @@ __device__ __forceinline__ Run run_at(const Params& p, int r, int bn) {
     R.mt0 = seg * p.run;
     R.len = min(p.run, p.tiles_m - R.mt0);
   } else {
-    const int rest = r / p.tiles_n;
-    R.n0 = (r - rest * p.tiles_n) * bn;
-    R.mt0 = rest % p.tiles_m;
-    R.z = rest / p.tiles_m;
+    const int per_z = p.tiles_n * p.tiles_m;
+    R.z = r / per_z;
+    const int rest = r - R.z * per_z;
+    if (p.group > 1) {
+      // groups of `group` m-tiles; inside a group m runs fastest, then n
+      const int grp = rest / (p.group * p.tiles_n);
+      const int m0 = grp * p.group;
+      const int gm = min(p.group, p.tiles_m - m0);
+      const int within = rest - grp * p.group * p.tiles_n;
+      R.n0 = (within / gm) * bn;
+      R.mt0 = m0 + within % gm;
+    } else {
+      R.n0 = (rest % p.tiles_n) * bn;
+      R.mt0 = rest / p.tiles_n;
+    }
     R.len = 1;
   }
   return R;
@@ -849,6 +861,24 @@ int run_simt(const GemmArgs& g, cudaStream_t s) {
   return check_launch("gemm_simt_kernel");
 }
 
+// Order of the streaming tile walk.  The persistent CTAs work on about
+// sm_count consecutive tiles at a time and move through K at similar speed,
+// so what one K slab of those tiles reads from L2 and DRAM is their distinct
+// A row blocks and B column blocks.  In row-band order (n fastest) a wave of
+// 148 tiles of an 8192^3 GEMM spans 4.6 row bands and all 32 column blocks,
+// so every wave streams the whole of B (256 MB) from DRAM: 4.7 GB of DRAM
+// reads per launch against 0.5 GB of operands (ncu).  Groups of G m-tiles
+// walked m-fastest make a wave ~G x 148/G tiles; the A + B bytes of a wave,
+// G * BM + (148 / G) * BN rows of K, are smallest near G = sqrt(148 BN / BM)
+// = 17.  Only long-K walks with many row bands are regrouped; the B-resident
+// small-K form has its own run order.
+int tile_group(int tiles_m, int tiles_n, int nk, int bn) {
+  constexpr int G = 16;
+  if (nk < 64 || tiles_m <= G || tiles_n <= 2) return 1;
+  (void)bn;
+  return G;
+}
+
 // splits > 1: partial tiles go to `ws` and are reduced into C afterwards.
 // reduce_into_c false (single-matrix GEMMs only): the partial tiles
 // [splits][M][N] stay in `ws` (one split: C itself goes to ws) and no
@@ -912,6 +942,7 @@ int run_gemm(const GemmArgs& g, int splits, float* ws, cudaStream_t s, bool redu
   p.tiles_n = (int)grid.x;
   p.tiles_m = (int)grid.y;
   p.tiles_z = (int)grid.z;
+  p.group = tile_group(p.tiles_m, p.tiles_n, nk, BN);
   // persistent: one CTA per SM (the shared memory and TMEM footprints allow no more)
   const int64_t ntiles = (int64_t)grid.x * grid.y * grid.z;
   KB_REQUIRE(ntiles <= 0x7fffffff, KB_ERR_UNSUPPORTED, "gemm: too many tiles");
