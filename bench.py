@@ -78,6 +78,10 @@ FALLBACK_BF16_TFLOPS = 1590.0
 TF32_CEILING_TFLOPS = 758.8
 L2_BYTES = 126 * 1024 * 1024
 FLUSH_BYTES = 256 * 1024 * 1024
+# CPU reference samples: at least 4x the host's last-level cache and this
+# many bytes per op; contractions about this many useful FLOPs
+MIN_SAMPLE_BYTES = 256 << 20
+SAMPLE_FLOPS = 2.0e11
 
 # kernels of ours launched per op call (for gpu_launches)
 LAUNCHES = {"gelu_tanh": 1, "gelu_erf": 1, "swish": 1, "relu": 1, "layer_norm": 1, "rms_norm": 1,
@@ -565,8 +569,8 @@ def cpu_reference(ops: list[str], steps: int, warmup: int, threads: int, peaks: 
 
     torch.set_num_threads(threads)
     llc, llc_how = host_llc_bytes()
-    target_bytes = max(4 * llc, 256 << 20)
-    target_flops = 2.0e11
+    target_bytes = max(4 * llc, MIN_SAMPLE_BYTES)
+    target_flops = SAMPLE_FLOPS
     models, desc = [], []
     roof_s, sample_bytes = 0.0, 0.0
     for name in ops:

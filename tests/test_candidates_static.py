@@ -101,3 +101,85 @@ def test_static_check_catches_fallbacks():
 def test_every_problem_has_a_candidate():
     for name in problems.SUBSET:
         assert candidate_path(name).exists(), name
+
+
+def _lib_symbols_of_entry(entry: str) -> set[str]:
+    """The C-ABI symbols an ENTRY of kbb200.ext reaches: the kbb200.ops
+    functions its body calls, and the LIB.kb_* functions (or "kb_*" names
+    passed to getattr(LIB, ...)) those bodies call — read from the sources'
+    syntax trees, so no GPU is needed."""
+    import ast
+
+    pkg = Path(__file__).resolve().parent.parent / "kernelbench-hip_b200" / "kbb200"
+
+    def funcs(path):
+        tree = ast.parse(path.read_text())
+        return {n.name: n for n in tree.body if isinstance(n, ast.FunctionDef)}
+
+    ext_f, ops_f = funcs(pkg / "ext.py"), funcs(pkg / "ops.py")
+
+    def ops_called(fn):
+        out = set()
+        for n in ast.walk(fn):
+            if isinstance(n, ast.Call) and isinstance(n.func, ast.Attribute) and \
+                    isinstance(n.func.value, ast.Name) and n.func.value.id == "ops":
+                out.add(n.func.attr)
+        return out
+
+    def lib_syms(name, seen):
+        if name in seen or name not in ops_f:
+            return set()
+        seen.add(name)
+        out = set()
+        for n in ast.walk(ops_f[name]):
+            if isinstance(n, ast.Attribute) and isinstance(n.value, ast.Name) and n.value.id == "LIB":
+                out.add(n.attr)
+            if isinstance(n, ast.Constant) and isinstance(n.value, str) and n.value.startswith("kb_"):
+                out.add(n.value)
+            if isinstance(n, ast.Call) and isinstance(n.func, ast.Name) and n.func.id in ops_f:
+                out |= lib_syms(n.func.id, seen)
+        return out
+
+    def direct(fn):  # LIB.kb_* used (or named) in the function's own body
+        out = set()
+        for n in ast.walk(fn):
+            if isinstance(n, ast.Attribute) and isinstance(n.value, ast.Name) and n.value.id == "LIB":
+                out.add(n.attr)
+            if isinstance(n, ast.Constant) and isinstance(n.value, str) and n.value.startswith("kb_"):
+                out.add(n.value)
+        return out
+
+    def ext_syms(name, seen):
+        if name in seen or name not in ext_f:
+            return set()
+        seen.add(name)
+        fn = ext_f[name]
+        out = direct(fn)
+        for o in ops_called(fn):
+            out |= lib_syms(o, set())
+        for n in ast.walk(fn):  # entries that delegate to another entry
+            if isinstance(n, ast.Call) and isinstance(n.func, ast.Name) and n.func.id in ext_f:
+                out |= ext_syms(n.func.id, seen)
+        return out
+
+    return ext_syms(entry, set())
+
+
+@pytest.mark.parametrize("name", problems.SUBSET)
+def test_entry_reaches_exported_c_abi_symbols(name):
+    """Every candidate's ENTRY resolves, through kbb200.ext and kbb200.ops, to
+    compute entries of the C ABI that include/kbb200.h declares and
+    libkbb200.so exports (not to a torch fallback)."""
+    import subprocess
+
+    from kbb200 import _lib
+
+    entry = candidate_entry(candidate_path(name).read_text())
+    syms = {s for s in _lib_symbols_of_entry(entry) if not s.endswith("_workspace_size")}
+    assert syms, f"{entry} reaches no kb_* compute entry"
+    header = (Path(__file__).resolve().parent.parent / "include" / "kbb200.h").read_text()
+    exported = subprocess.run(["nm", "-D", "--defined-only", str(_lib.LIB_PATH)], capture_output=True,
+                              text=True, check=True).stdout.split()
+    for s in syms:
+        assert s in exported, f"{entry} -> {s} is not exported by libkbb200.so"
+        assert f" {s}(" in header, f"{entry} -> {s} is not declared in include/kbb200.h"
