@@ -447,6 +447,126 @@ __global__ void __launch_bounds__(NT) row_persist_kernel(RowArgs a) {
     asm volatile("barrier.cluster.arrive.relaxed.aligned;\n\tbarrier.cluster.wait.aligned;" ::: "memory");
 }
 
+// The same persistent walk with the prefetch in two halves.  With one
+// buffer for the whole row segment, the next row's copy can start only after
+// every thread has moved the whole current row into registers, so each SM's
+// read stream pauses for that copy-out and barrier once per row — a pause
+// measured in SM cycles, which made these kernels slow down with the SM
+// clock under the power cap.  Here the segment buffer is two halves with a
+// barrier each: as soon as the first half has been read out, the next row's
+// first half is already being fetched while the second half is read out.
+// Each thread's first VPT/2 vectors lie in the first half (vec_slot), so the
+// register layout and the math are unchanged.
+template <RowOp OP, int NT, int VPT, int CL, bool PAIRED>
+__global__ void __launch_bounds__(NT) row_persist_halves_kernel(RowArgs a) {
+  extern __shared__ float4 seg_buf[];  // one row segment: [first half | second half]
+  __shared__ float red[64];
+  __shared__ float slots[4];
+  __shared__ __align__(8) uint64_t bars[2];
+  constexpr int H = VPT / 2;
+  int rank = 0;
+  if constexpr (CL > 1) rank = (int)cg::this_cluster().block_rank();
+  const int64_t cluster_id = blockIdx.x / CL, nclusters = gridDim.x / CL;
+  const int seg4 = a.cols / 4 / CL;
+  const int half4 = min(seg4, H * NT);  // float4s in the first half
+  const int rest4 = seg4 - half4;       // in the second (0: one half only)
+  const int64_t col4_base = (int64_t)rank * seg4;
+  const float* xseg = a.x + col4_base * 4;
+  if (threadIdx.x == 0) {
+    for (int d = 0; d < 2; ++d)
+      asm volatile("mbarrier.init.shared::cta.b64 [%0], 1;" ::"r"(smem_addr(&bars[d])) : "memory");
+    asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
+  }
+  __syncthreads();
+  if constexpr (CL > 1) cg::this_cluster().sync();  // peers' shared memory exists from here on
+  if (threadIdx.x == 0 && cluster_id < a.rows) {
+    const float* src = xseg + cluster_id * (int64_t)a.cols;
+    bulk_load(smem_addr(seg_buf), src, (uint32_t)half4 * 16u, smem_addr(&bars[0]));
+    if (rest4 > 0) bulk_load(smem_addr(seg_buf + half4), src + (int64_t)half4 * 4, (uint32_t)rest4 * 16u,
+                             smem_addr(&bars[1]));
+  }
+  bool alive = true;
+  ClusterReducer<NT, CL> r{red, slots};
+  int64_t i = 0;
+  for (int64_t row = cluster_id; row < a.rows; row += nclusters, ++i) {
+    const uint32_t parity = (uint32_t)(i & 1);
+    const int64_t next = row + nclusters;
+    const float* nsrc = xseg + next * (int64_t)a.cols;
+    float4 v[VPT];
+    bool ok[VPT];
+    // first half: read out, then refill it with the next row's first half
+    bool got = alive ? wait_bounded(smem_addr(&bars[0]), parity) : true;
+#pragma unroll
+    for (int k = 0; k < H; ++k) {
+      const int64_t j = vec_slot<PAIRED>(k, threadIdx.x, NT);
+      ok[k] = j < seg4;
+      v[k] = (ok[k] && alive && got) ? seg_buf[j] : make_float4(0.f, 0.f, 0.f, 0.f);
+    }
+    bool all = __syncthreads_and(got) != 0;
+    if (threadIdx.x == 0 && alive && all && next < a.rows)
+      bulk_load(smem_addr(seg_buf), nsrc, (uint32_t)half4 * 16u, smem_addr(&bars[0]));
+    // second half
+    got = (alive && all && rest4 > 0) ? wait_bounded(smem_addr(&bars[1]), parity) : true;
+#pragma unroll
+    for (int k = H; k < VPT; ++k) {
+      const int64_t j = vec_slot<PAIRED>(k, threadIdx.x, NT);
+      ok[k] = j < seg4;
+      v[k] = (ok[k] && alive && all && got) ? seg_buf[j] : make_float4(0.f, 0.f, 0.f, 0.f);
+    }
+    all = (__syncthreads_and(got) != 0) && all;
+    if (threadIdx.x == 0 && alive && all && rest4 > 0 && next < a.rows)
+      bulk_load(smem_addr(seg_buf + half4), nsrc + (int64_t)half4 * 4, (uint32_t)rest4 * 16u,
+                smem_addr(&bars[1]));
+    if (!all && alive) {
+      alive = false;
+      if (threadIdx.x == 0) atomicExch(&g_row_fault, 1);
+    }
+    float4* ys = reinterpret_cast<float4*>(a.y + row * (int64_t)a.cols) + col4_base;
+    row_math<OP, VPT, PAIRED>(v, ok, a, ys, col4_base, NT, threadIdx.x, r, alive);
+  }
+  if constexpr (CL > 1)
+    asm volatile("barrier.cluster.arrive.relaxed.aligned;\n\tbarrier.cluster.wait.aligned;" ::: "memory");
+}
+
+template <RowOp OP, int NT, int VPT, int CL, bool PAIRED>
+cudaError_t launch_halves_impl(const RowArgs& a, cudaStream_t s) {
+  auto kern = row_persist_halves_kernel<OP, NT, VPT, CL, PAIRED>;
+  const int smem = a.cols / CL * 4;
+  static uint64_t attr_set = 0;
+  int dev = 0;
+  cudaGetDevice(&dev);
+  if (dev < 64 && !(attr_set >> dev & 1)) {
+    cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, 200 * 1024);
+    if (e != cudaSuccess) return e;
+    attr_set |= 1ull << dev;
+  }
+  cudaLaunchConfig_t cfg = {};
+  cfg.blockDim = dim3(NT);
+  cfg.dynamicSmemBytes = smem;
+  cfg.stream = s;
+  cudaLaunchAttribute attr[1];
+  attr[0].id = cudaLaunchAttributeClusterDimension;
+  attr[0].val.clusterDim.x = CL;
+  attr[0].val.clusterDim.y = 1;
+  attr[0].val.clusterDim.z = 1;
+  cfg.attrs = attr;
+  cfg.numAttrs = 1;
+  int nclusters = 0;
+  cfg.gridDim = dim3(CL * 148);
+  cudaError_t e = cudaOccupancyMaxActiveClusters(&nclusters, kern, &cfg);
+  if (e != cudaSuccess || nclusters <= 0) nclusters = sm_count() / CL;
+  nclusters = (int)std::max<int64_t>(1, std::min<int64_t>(nclusters, a.rows));
+  cfg.gridDim = dim3((unsigned)(nclusters * CL));
+  return cudaLaunchKernelEx(&cfg, kern, a);
+}
+
+template <RowOp OP, int NT, int VPT, int CL>
+cudaError_t launch_halves(const RowArgs& a, cudaStream_t s) {
+  if (aligned32(a.x) && aligned32(a.y) && a.cols % (8 * CL) == 0)
+    return launch_halves_impl<OP, NT, VPT, CL, true>(a, s);
+  return launch_halves_impl<OP, NT, VPT, CL, false>(a, s);
+}
+
 template <RowOp OP, int NT, int VPT, int CL, int DEPTH, bool PAIRED>
 cudaError_t launch_persist_impl(const RowArgs& a, cudaStream_t s) {
   auto kern = row_persist_kernel<OP, NT, VPT, CL, DEPTH, PAIRED>;
@@ -615,8 +735,8 @@ int launch_rows(const char* name, const RowArgs& a, cudaStream_t s) {
     e = launch_block<OP, 512, 8, 1>(a, s);
   } else if (c <= 32768) {
     // one persistent 1024-thread CTA per SM: the row in registers, the next
-    // row streaming into shared memory
-    e = launch_persist<OP, 1024, 8, 1, 1>(a, s);
+    // row streaming into shared memory in two halves
+    e = launch_halves<OP, 1024, 8, 1>(a, s);
   } else if (c <= 65536 && c % 8 == 0) {
     e = launch_persist<OP, 1024, 8, 2, 1>(a, s);
   } else if (c % 16 == 0) {

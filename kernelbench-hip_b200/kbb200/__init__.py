@@ -5,12 +5,13 @@ candidate API.
     y = kbb200.ops.gelu_tanh(x)          # tensor-level API
     kbb200.ext.mingpt_gelu_entry(x, y)   # candidate entry names (EXT.<ENTRY>)
 
-The submodules that launch kernels (`ops`, `ext`, `dist`, `p2p`, `_lib`) load
-libkbb200.so (C ABI, include/kbb200.h) when they are first imported and fail
-if it has not been built; there is no other implementation to fall back to.
-Importing the package itself, or its pure-host modules (`workloads`,
-`launch`), loads nothing, so a process that only plans or sweeps work (the
-CPU reference timing, the multi-GPU launcher) never maps the library.
+The submodules that launch kernels (`ops`, `ext`, `p2p`, `_lib`) load
+libkbb200.so (C ABI, include/kbb200.h) when they are first imported, and
+`dist` when it first calls a kernel; they fail if it has not been built, and
+there is no other implementation to fall back to.  Importing the package
+itself, or its pure-host modules (`workloads`, `launch`, `milestone_table`),
+loads nothing, so a process that only plans or sweeps work (the CPU
+reference timing, the multi-GPU launcher) never maps the library.
 """
 from __future__ import annotations
 
@@ -18,7 +19,7 @@ import importlib
 
 __version__ = "0.2.0"
 
-_SUBMODULES = {"_lib", "ops", "ext", "dist", "p2p", "workloads", "launch"}
+_SUBMODULES = {"_lib", "ops", "ext", "dist", "p2p", "workloads", "launch", "milestone_table"}
 _FROM_LIB = {"LIB", "KbError", "LIB_PATH"}
 
 

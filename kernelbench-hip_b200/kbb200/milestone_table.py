@@ -6,7 +6,7 @@ the GPU count of the verdict, GB/s or TFLOP/s of the whole job, fraction of
 the measured per-GPU roofline, and the torch-eager CPU estimate with its core
 count.
 
-    python tests/milestone_table.py verdicts/ [--md out.md] [--json out.json]
+    python -m kbb200.milestone_table verdicts/ [--md out.md] [--json out.json]
 """
 from __future__ import annotations
 

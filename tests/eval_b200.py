@@ -75,8 +75,9 @@ def _peaks() -> dict:
     return {"hbm_gbs": 6650.0, "source": "fallback"}
 
 
-# 3xTF32 ceiling: torch's TF32 dense burst on this pool (8192^3) divided by 3
-TF32_BURST_TFLOPS = 758.8
+# 3xTF32 ceiling: the bench's TF32 figure (cuBLAS TF32 8192^3 burst from its
+# probe, bench.measure_tf32_tflops) divided by 3 — one denominator for both
+from bench import TF32_CEILING_TFLOPS as TF32_BURST_TFLOPS  # noqa: E402
 
 
 def clear_l2(device, nbytes: int) -> None:

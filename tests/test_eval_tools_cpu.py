@@ -6,7 +6,7 @@ import json
 
 
 def test_table_from_verdicts(tmp_path):
-    from tests.milestone_table import load, markdown, rows
+    from kbb200.milestone_table import load, markdown, rows
 
     (tmp_path / "a.json").write_text(json.dumps({
         "problem": "40_LayerNorm", "milestone": 2, "cand_time": {"median_ms": 0.63},

@@ -23,7 +23,7 @@ def test_eval_small(name, cuda_device, tmp_path):
 
 def test_milestone_table(cuda_device, tmp_path):
     from tests.eval_b200 import evaluate
-    from tests.milestone_table import load, markdown, rows
+    from kbb200.milestone_table import load, markdown, rows
 
     for name in ("19_ReLU", "40_LayerNorm"):
         evaluate(name, str(tmp_path / f"{name}.json"), small=True, trials=3, with_cpu=False)
