@@ -14,7 +14,9 @@ For MSE, Frobenius and BatchNorm the exchange is fused into the kernel that
 computes the shard's partial (`mse_loss`, `sumsq`, `batch_norm_stats`): the
 CTA that finishes the partial pass last pushes the folded values to every
 peer and sums what arrived, so partial, all-reduce and finish are one
-launch.  Those calls reuse one zeroed workspace owned by the communicator.
+launch.  Those calls reuse one zeroed workspace owned by the communicator,
+so a communicator serves one stream at a time (its calls are ordered on the
+stream anyway: every rank makes the same calls in the same order).
 
 Every rank must make the same calls in the same order.  A wait that runs
 past `timeout_s` makes the kernel record a fault and write NaN as its

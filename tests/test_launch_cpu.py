@@ -115,3 +115,21 @@ def test_family_cell_efficiency_per_op():
     assert r["parallel_eff"] == pytest.approx(20.0 / (8 * 2.7), abs=1e-4)
     assert r["per_op_parallel_eff"]["matmul"] == pytest.approx(5.0 / 5.6, abs=1e-4)
     assert r["per_op_parallel_eff"]["mse_loss"] == pytest.approx(0.8, abs=1e-4)
+
+
+def test_eval_cells_read_the_verdict_file(tmp_path):
+    """Eval cells take their record from the verdict file the eval writes; a
+    cell whose eval exits non-zero keeps the verdict's reason and gets -1."""
+    from kbb200.launch import sweep
+
+    def command(kind, op, ngpu, out_file):
+        ms = -1 if op == "bad" else 1
+        body = (f"import json, sys; json.dump({{'problem': {op!r}, 'milestone': {ms}, 'why': 'parity failed' "
+                f"if {ms} < 0 else None, 'cand_time': {{'median_ms': 0.5}}}}, open({str(out_file)!r}, 'w')); "
+                f"sys.exit(0 if {ms} > 0 else 1)")
+        return [sys.executable, "-c", body]
+
+    res = sweep("eval", ["good", "bad"], [1], tmp_path / "e.json", timeout_s=60.0, steps=1, warmup=1,
+                command=command)
+    assert res["good@1gpu"]["milestone"] == 1 and res["good@1gpu"]["cand_time"]["median_ms"] == 0.5
+    assert res["bad@1gpu"]["milestone"] == -1 and res["bad@1gpu"]["why"] == "parity failed"
