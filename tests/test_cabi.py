@@ -104,3 +104,40 @@ def test_argmax_rejects_empty_reduced_dim():
     from kbb200 import LIB
 
     assert LIB.kb_argmax_dim1_f32(None, 1, 2, 0, 3, None) == 1
+
+
+def test_a_c_program_compiles_links_and_calls_the_abi(tmp_path):
+    """The header is plain C: a C translation unit includes it, links
+    -lkbb200 and calls host-side entries (no GPU needed for these), as a
+    non-Python host would."""
+    import os
+    import subprocess
+
+    from kbb200 import _lib
+
+    src = tmp_path / "abi.c"
+    src.write_text(r'''
+#include <stdio.h>
+#include "kbb200.h"
+int main(void) {
+  const char* s = kb_status_string(KB_ERR_WORKSPACE);
+  size_t ws = kb_sharded_workspace_size();
+  size_t buf = kb_p2p_buffer_bytes(16, 8);
+  size_t mse = kb_mse_workspace_size(1000);
+  int st = kb_gelu_tanh_f32(0, 0, -1, 0);   /* negative size: rejected on the host */
+  printf("%d %s %zu %zu %zu %d\n", kb_version(), s, ws, buf, mse, st);
+  return 0;
+}
+''')
+    lib_dir = _lib.LIB_PATH.parent
+    exe = tmp_path / "abi"
+    cuda_inc = "/usr/local/cuda/include"
+    r = subprocess.run(["gcc", "-std=c99", "-I", str(REPO / "include"), "-I", cuda_inc, str(src), "-L", str(lib_dir),
+                        "-lkbb200", "-o", str(exe)], capture_output=True, text=True)
+    assert r.returncode == 0, r.stderr
+    env = dict(os.environ, LD_LIBRARY_PATH=f"{lib_dir}:{os.environ.get('LD_LIBRARY_PATH', '')}")
+    out = subprocess.run([str(exe)], capture_output=True, text=True, env=env, timeout=60)
+    assert out.returncode == 0, out.stderr
+    ver, *rest = out.stdout.split()
+    assert int(ver) > 0 and int(rest[-1]) == 1  # KB_ERR_INVALID_ARG
+    assert int(rest[-4]) == 256 + 2048 * 8 and int(rest[-3]) == 4096 + 2 * 8 * 256
