@@ -22,18 +22,21 @@ MAX_RANKS = 64  # flags[2][64] uint32 at byte 0 of each buffer (csrc/p2p.cu)
 
 
 class Emulated:
-    """Rank 0 of a world of 2 whose rank 1 is played by the host."""
+    """Rank 0 of a world of `world` ranks whose other ranks are played by the
+    host: one buffer per rank on this GPU (rank 0 pushes into all of them),
+    and the peers' parts and flags written into rank 0's buffer before the
+    launch."""
 
-    def __init__(self, device, payload_bytes=1 << 16):
+    def __init__(self, device, payload_bytes=1 << 16, world=2):
         from kbb200._lib import LIB, check
 
         self.LIB, self.check = LIB, check
-        self.world = 2
+        self.world = world
         self.buf_bytes = LIB.kb_p2p_buffer_bytes(payload_bytes, self.world)
         self.hdr = LIB.kb_p2p_header_bytes()
         self.cap = ((self.buf_bytes - self.hdr) // 2 // self.world) & ~255  # bytes per rank part
         self.ptrs = []
-        for _ in range(2):
+        for _ in range(world):
             p = C.c_void_p()
             check("alloc", LIB.kb_p2p_buffer_alloc(self.buf_bytes, C.byref(p)))
             self.ptrs.append(p.value)
@@ -51,12 +54,13 @@ class Emulated:
         assert err == rt.cudaError_t.cudaSuccess, err
         torch.cuda.synchronize()
 
-    def set_peer(self, epoch: int, data: torch.Tensor) -> None:
-        """What rank 1 would push into our buffer (part 1 of slot epoch & 1)."""
+    def set_peer(self, epoch: int, data: torch.Tensor, peer: int = 1) -> None:
+        """What rank `peer` would push into our buffer (part `peer` of slot
+        epoch & 1), and its ready flag."""
         slot = epoch & 1
-        self.write(self.ptrs[0] + self.hdr + (slot * self.world + 1) * self.cap, data)
+        self.write(self.ptrs[0] + self.hdr + (slot * self.world + peer) * self.cap, data)
         flag = torch.tensor([epoch], dtype=torch.int32, device=self.device)
-        self.write(self.ptrs[0] + (slot * MAX_RANKS + 1) * 4, flag)
+        self.write(self.ptrs[0] + (slot * MAX_RANKS + peer) * 4, flag)
 
     def close(self) -> None:
         torch.cuda.synchronize()
@@ -154,5 +158,29 @@ def test_bad_arguments_are_rejected(cuda_device):
         st = em.LIB.kb_p2p_allreduce_f64(em.bufs.data_ptr(), 0, 2, em.buf_bytes, x.data_ptr(), x.data_ptr(),
                                          big, 1, 1_000_000, _stream())
         assert st != 0
+    finally:
+        em.close()
+
+
+@pytest.mark.parametrize("world", [4, 8])
+def test_allreduce_many_ranks_rank_ordered(world, cuda_device):
+    """Rank 0 of 4 and 8 ranks: the standalone peer all-reduce sums every
+    rank's part in rank order (the other ranks played by the host)."""
+    em = Emulated(cuda_device, world=world)
+    try:
+        n = 3000
+        mine = torch.randn(n, dtype=torch.float64, device=cuda_device)
+        parts = [torch.randn(n, dtype=torch.float64, device=cuda_device) for _ in range(1, world)]
+        for p, t in enumerate(parts, start=1):
+            em.set_peer(3, t, peer=p)
+        out = torch.empty_like(mine)
+        em.check("allreduce", em.LIB.kb_p2p_allreduce_f64(em.bufs.data_ptr(), 0, world, em.buf_bytes,
+                                                          mine.data_ptr(), out.data_ptr(), n, 3, 2_000_000_000,
+                                                          _stream()))
+        assert _fault() == 0
+        want = torch.zeros_like(mine) + mine
+        for t in parts:
+            want = want + t
+        assert torch.equal(out, want)
     finally:
         em.close()

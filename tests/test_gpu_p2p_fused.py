@@ -134,3 +134,50 @@ def test_fused_rejects_oversized_exchange(cuda_device):
         assert st != 0 and b"exceeds" in em.LIB.kb_last_error()
     finally:
         em.close()
+
+
+@pytest.mark.parametrize("world", [4, 8])
+def test_fused_exchange_with_many_ranks(world, cuda_device):
+    """Rank 0 of 4 and 8 ranks (the others played by the host): the slot
+    layout for that world size, the wait for every peer's flag, and the sum
+    in rank order over all parts, for the MSE and BatchNorm exchanges."""
+    from kbb200 import ops
+
+    em = Emulated(cuda_device, payload_bytes=1 << 16, world=world)
+    try:
+        ws = _ws(em, max(em.LIB.kb_sharded_workspace_size(), em.LIB.kb_batchnorm_sharded_workspace_size(8, 128, 1024)))
+        g = torch.Generator(device=cuda_device).manual_seed(world)
+        a = torch.randn(1 << 20, device=cuda_device, generator=g)
+        b = torch.randn(1 << 20, device=cuda_device, generator=g)
+        peers = [torch.tensor([float(10 * p), float(p)], dtype=torch.float64, device=cuda_device)
+                 for p in range(1, world)]
+        for p, t in enumerate(peers, start=1):
+            em.set_peer(1, t, peer=p)
+        out = torch.empty((), device=cuda_device)
+        em.check("mse", em.LIB.kb_mse_sharded_f32(a.data_ptr(), b.data_ptr(), out.data_ptr(), a.numel(),
+                                                  ws.data_ptr(), ws.numel(), em.bufs.data_ptr(), 0, world,
+                                                  em.buf_bytes, 1, WAIT_NS, _stream()))
+        assert _fault() == 0
+        local = ops.mse_partial(a, b)
+        tot = float(local[0])
+        cnt = float(local[1])
+        for t in peers:  # rank order
+            tot += float(t[0])
+            cnt += float(t[1])
+        assert float(out) == pytest.approx(tot / cnt, rel=1e-6)
+
+        x = torch.randn(8, 128, 32, 32, device=cuda_device, generator=g)
+        pst = [torch.rand(257, dtype=torch.float64, device=cuda_device, generator=g) for _ in range(1, world)]
+        for p, t in enumerate(pst, start=1):
+            em.set_peer(2, t, peer=p)
+        stats = torch.empty(257, dtype=torch.float64, device=cuda_device)
+        em.check("bn", em.LIB.kb_batchnorm_stats_sharded_f64(x.data_ptr(), stats.data_ptr(), 8, 128, 1024,
+                                                             ws.data_ptr(), ws.numel(), em.bufs.data_ptr(), 0,
+                                                             world, em.buf_bytes, 2, WAIT_NS, _stream()))
+        assert _fault() == 0
+        want = ops.batch_norm_stats(x)
+        for t in pst:
+            want = want + t
+        torch.testing.assert_close(stats, want, rtol=1e-12, atol=1e-9)
+    finally:
+        em.close()
