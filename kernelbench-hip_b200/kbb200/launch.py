@@ -197,6 +197,13 @@ def markdown(results: dict) -> str:
         ok = "ok" if r.get("milestone", -1) >= 0 else f"-1 ({r.get('why', '')[:60]})"
         rows.append(f"| {key} | {ok} | {r.get('ms_per_step', '')} | {r.get('value', '')} | "
                     f"{r.get('parallel_eff', '')} | {r.get('wall_s', '')} |")
+    # per-op efficiency of family cells, one column per GPU count
+    fam = [(k, r) for k, r in results.items() if r.get("per_op_parallel_eff")]
+    if fam:
+        ops = list(fam[0][1]["per_op_parallel_eff"])
+        rows += ["", "| op | " + " | ".join(k for k, _ in fam) + " |", "|---|" + "---|" * len(fam)]
+        for o in ops:
+            rows.append(f"| {o} | " + " | ".join(str(r["per_op_parallel_eff"].get(o, "")) for _, r in fam) + " |")
     return "\n".join(rows) + "\n"
 
 
