@@ -206,9 +206,9 @@ KB_API int kb_batchnorm_apply_f32(const float* x, const float* gamma,
 KB_API int kb_sgemm_3xtf32(const float* A, const float* B, float* C, int64_t M,
                     int64_t N, int64_t K, int64_t lda, int64_t ldb,
                     int64_t ldc, int trans_a, kbStream stream);
-/* The same GEMM with a caller workspace: when the output tiles fill the
- * persistent grid's waves badly (e.g. a 1024 x 8192 row shard of an 8192^3
- * GEMM: 256 tiles on 148 SMs), K is split into s parts whose partial tiles
+/* The same GEMM with a caller workspace: when the output has fewer tiles
+ * than the GPU has SMs (e.g. a 256-row strip of an 8192-wide, 8192-deep
+ * GEMM: 64 tiles on 148 SMs), K is split into s parts whose partial tiles
  * go to the workspace and are summed in a fixed order (deterministic).
  * kb_sgemm_workspace_size returns s * M * N * 4 bytes, or 0 when no split
  * pays; a smaller workspace runs the GEMM unsplit.  trans_a is never split.

@@ -981,20 +981,25 @@ int splitk_count(int64_t M, int64_t N, int64_t K, int sms) {
   return (int)sp;
 }
 
-// K splits for a plain GEMM whose tiles fill the persistent grid badly.
-// The CTAs walk the tiles in waves of `sms`; a GEMM with 1.73 waves of
-// tiles (a 1024 x 8192 row shard of 8192^3 on 8 GPUs: 256 tiles on 148
-// SMs) pays for 2 full waves.  Cutting K into s splits gives s x tiles
-// shorter work units that fill the waves more evenly; it costs one partial
-// tile per split in memory, a deterministic reduction pass (s + 1 reads and
-// writes of C's size) and a per-unit pipeline fill.  Model, per SM: a 16-deep
-// K block takes t_kb (0.68 us measured at 8192^3 in steady state), a work
-// unit t_unit more; the reduction runs at HBM speed.  The split is taken when
-// the model saves at least 3 %.
+// K splits for a plain GEMM whose tiles leave most of the persistent grid
+// idle: fewer output tiles than SMs (a 256-row strip of an 8192-wide,
+// 8192-deep GEMM has 64 tiles for 148 SMs).  Cutting K into s splits gives
+// s x tiles shorter work units; it costs one partial tile per split in
+// memory, a deterministic reduction pass (s + 1 reads and writes of C's
+// size) and a per-unit pipeline fill.  Model, per SM: a 16-deep K block
+// takes t_kb (0.68 us measured at 8192^3 in steady state), a work unit t_unit
+// more; the reduction runs at HBM speed.  The split is taken when the model
+// saves at least 3 %.  Grids of a wave or more are never split: measured on
+// a 1024 x 8192 x 8192 row shard (256 tiles, 1.73 waves), the split into 4
+// was 2.7 % slower than the unsplit walk (0.651 vs 0.634 ms) — the SMs of
+// a partial last wave run faster than the model assumes (the chip is power-
+// and L2-limited, and fewer busy SMs share both), and at 256 rows
+// (0.43 waves) the split into 2 was 1.75x faster (0.210 vs 0.367 ms).
 int wave_splits(int64_t M, int64_t N, int64_t K, int sms) {
   constexpr double t_kb = 0.68e-6, t_unit = 2.0e-6, t_launch = 5.0e-6, hbm = 6.4e12;
   const int64_t tiles = ceil_div(M, BM) * ceil_div(N, N > 128 ? 256 : 128);
   const int64_t nk = ceil_div(K, BK);
+  if (tiles >= sms) return 1;
   auto model = [&](int sp) {
     const int64_t kbps = ceil_div(nk, sp);
     const int64_t units = tiles * ceil_div(nk, kbps);

@@ -368,10 +368,10 @@ def test_gemm_b_resident_small_k(shape, cuda_device):
 
 @pytest.mark.parametrize("mnk", [(1024, 8192, 8192), (256, 8192, 8192), (2048, 4096, 1024), (300, 520, 4096)])
 def test_sgemm_wave_split(mnk, cuda_device):
-    """Shapes whose tiles fill the persistent grid's waves badly take the K
-    split (kb_sgemm_3xtf32_ws; the first is one row shard of the 8192^3 GEMM
-    on 8 GPUs): fp32-level error, deterministic, and close to the unsplit
-    entry on the same operands."""
+    """Shapes with fewer output tiles than SMs take the K split
+    (kb_sgemm_3xtf32_ws); a row shard of the 8192^3 GEMM on 8 GPUs (256
+    tiles) does not.  Either way: fp32-level error, deterministic, and close
+    to the unsplit entry on the same operands."""
     import ctypes as C
 
     from kbb200 import ops as K
@@ -382,8 +382,10 @@ def test_sgemm_wave_split(mnk, cuda_device):
     A = torch.randn(M, Kd, device=cuda_device, generator=g) / Kd ** 0.5
     B = torch.randn(Kd, N, device=cuda_device, generator=g)
     ws = LIB.kb_sgemm_workspace_size(M, N, Kd, 0)
-    if mnk[0] in (1024, 256):
-        assert ws > 0, "the row shard of 8192^3 should take the split"
+    if mnk[0] in (256, 300):
+        assert ws > 0, "fewer tiles than SMs: the K split pays"
+    if mnk[0] in (1024, 2048):
+        assert ws == 0, "a wave or more of tiles: no split"
     got = K.matmul(A, B)
     _gemm_check(got, A, B, f"wave split {mnk}")
     assert torch.equal(got, K.matmul(A, B)), "must be deterministic"
