@@ -645,7 +645,7 @@ def profile_op(op: str, frac: float, reps: int = 3) -> int:
 
 
 # ----------------------------------------------------------------- exchange sweep
-def exchange_sweep(iters: int) -> int:
+def exchange_sweep(iters: int, sink=None) -> int:
     """Per-call cost of the cross-GPU step of the sharded ops under torchrun:
     the library's peer-memory all-reduce (kbb200.p2p.PeerComm) against
     NCCL's all_reduce at the payloads the sharded ops exchange, plus the
@@ -706,7 +706,10 @@ def exchange_sweep(iters: int) -> int:
     finally:
         comm.close()
     if tdist.get_rank() == 0:
-        print(json.dumps(res), flush=True)
+        if sink is not None:
+            sink.emit(json.dumps(res))
+        else:
+            print(json.dumps(res), flush=True)
     tdist.barrier()
     tdist.destroy_process_group()
     return 0
@@ -773,7 +776,7 @@ def _main(sink) -> int:
     if a.profile_op:
         return profile_op(a.profile_op, a.frac)
     if a.exchange_sweep:
-        return exchange_sweep(a.iters)
+        return exchange_sweep(a.iters, sink)
     if a.warmup < 3 and a.impl == "ours":
         a.warmup = 3
 
