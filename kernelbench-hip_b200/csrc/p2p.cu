@@ -16,8 +16,9 @@
 //      its K-split partial tiles) is stored into slot s, part `rank`, of
 //      every rank's buffer — posted writes over NVLink;
 //   2. system-scope fence, then a grid barrier (bounded wait);
-//   3. CTA 0 publishes: system-scope release store of e into flags[s][rank]
-//      of every rank;
+//   3. CTA 0 publishes: a release of e into flags[s][rank] of every rank
+//      (one acq_rel fence per lane of warp 0, then relaxed system-scope
+//      stores, the lanes covering different ranks at the same time);
 //   4. every CTA waits (bounded) until its own flags[s][p] == e for every p;
 //   5. dst[i] = sum over p = 0 .. world-1 of part p of its own slot s, in
 //      rank order (local reads): every rank computes bit-identical results.
@@ -67,9 +68,6 @@ __device__ __forceinline__ uint64_t now_ns() {
   uint64_t t;
   asm volatile("mov.u64 %0, %%globaltimer;" : "=l"(t));
   return t;
-}
-__device__ __forceinline__ void store_release_sys(unsigned* p, unsigned v) {
-  asm volatile("st.release.sys.global.u32 [%0], %1;" ::"l"(p), "r"(v) : "memory");
 }
 __device__ __forceinline__ unsigned load_acquire_sys(const unsigned* p) {
   unsigned v;
@@ -135,32 +133,40 @@ __global__ void __launch_bounds__(kP2PThreads) p2p_allreduce_kernel(P2PArgs a) {
   // 2. the pushes are visible system-wide, then a grid barrier
   __threadfence_system();
   __syncthreads();
-  if (threadIdx.x == 0) {
+  if (threadIdx.x < 32) {
     bool ok = true;
-    if (gridDim.x > 1) {
-    const unsigned old = atomicAdd(&mine_h->bar_count, 1u);
-    if (old == gridDim.x - 1) {
-      mine_h->bar_count = 0;
-      __threadfence();
-      atomicExch(&mine_h->bar_gen, a.epoch);
-    } else {
-      ok = bounded_wait([&] { return load_volatile(&mine_h->bar_gen) == a.epoch; }, a.timeout_ns,
-                        (1 << 8) | a.rank);
+    if (threadIdx.x == 0 && gridDim.x > 1) {
+      const unsigned old = atomicAdd(&mine_h->bar_count, 1u);
+      if (old == gridDim.x - 1) {
+        mine_h->bar_count = 0;
+        __threadfence();
+        atomicExch(&mine_h->bar_gen, a.epoch);
+      } else {
+        ok = bounded_wait([&] { return load_volatile(&mine_h->bar_gen) == a.epoch; }, a.timeout_ns,
+                          (1 << 8) | a.rank);
+      }
     }
-    }
-    // 3. tell every rank that this rank's part has arrived
+    ok = __shfl_sync(0xffffffffu, ok ? 1 : 0, 0) != 0;
+    __syncwarp();  // orders lane 0's view of the grid barrier before every lane's fence
+    // 3. tell every rank that this rank's part has arrived: one acq_rel
+    //    fence per lane, then relaxed system-scope flag stores (a release
+    //    pattern), lane p signalling peers p, p + 32, ... in parallel
     if (ok && blockIdx.x == 0) {
       __threadfence_system();
-      for (int p = 0; p < a.world; ++p) {
+      asm volatile("fence.acq_rel.sys;" ::: "memory");
+      for (int p = threadIdx.x; p < a.world; p += 32) {
         Header* h = reinterpret_cast<Header*>(a.bufs[p]);
-        store_release_sys(&h->flags[slot][a.rank], a.epoch);
+        asm volatile("st.relaxed.sys.global.u32 [%0], %1;" ::"l"(&h->flags[slot][a.rank]), "r"(a.epoch)
+                     : "memory");
       }
     }
     // 4. wait for every rank's slot
-    for (int p = 0; ok && p < a.world; ++p)
-      ok = bounded_wait([&] { return load_acquire_sys(&mine_h->flags[slot][p]) == a.epoch; },
-                        a.timeout_ns, (2 << 8) | p);
-    s_ok = ok ? 1 : 0;
+    if (threadIdx.x == 0) {
+      for (int p = 0; ok && p < a.world; ++p)
+        ok = bounded_wait([&] { return load_acquire_sys(&mine_h->flags[slot][p]) == a.epoch; },
+                          a.timeout_ns, (2 << 8) | p);
+      s_ok = ok ? 1 : 0;
+    }
   }
   __syncthreads();
   T* dst = static_cast<T*>(a.dst);

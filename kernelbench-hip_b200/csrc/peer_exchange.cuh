@@ -10,8 +10,9 @@
 // all-reduce in p2p.cu:
 //   push   the values into slot (epoch & 1), part `rank`, of every rank's
 //          buffer (posted stores over NVLink), then a system-scope fence;
-//   flag   a system-scope release store of `epoch` into flags[slot][rank]
-//          of every rank;
+//   flag   a release (one acq_rel fence per lane, then relaxed system-scope
+//          stores, one peer per lane) of `epoch` into flags[slot][rank] of
+//          every rank;
 //   wait   (bounded by %globaltimer) until this rank's flags[slot][p] ==
 //          epoch for every p;
 //   sum    over p = 0 .. world-1 of part p, in rank order: bit-identical on
@@ -60,8 +61,14 @@ __device__ __forceinline__ uint64_t peer_now_ns() {
   return t;
 }
 
-__device__ __forceinline__ void peer_store_release(unsigned* p, unsigned v) {
-  asm volatile("st.release.sys.global.u32 [%0], %1;" ::"l"(p), "r"(v) : "memory");
+// A fence.acq_rel.sys followed by relaxed system-scope stores is a release
+// pattern for each of those stores (PTX memory model), so one fence per lane
+// covers all of a lane's flag stores, and the lanes of a warp store their
+// flags to different peers at the same time instead of one st.release
+// (one fence) after another.
+__device__ __forceinline__ void peer_fence_acq_rel() { asm volatile("fence.acq_rel.sys;" ::: "memory"); }
+__device__ __forceinline__ void peer_store_relaxed(unsigned* p, unsigned v) {
+  asm volatile("st.relaxed.sys.global.u32 [%0], %1;" ::"l"(p), "r"(v) : "memory");
 }
 
 __device__ __forceinline__ unsigned peer_load_acquire(const unsigned* p) {
@@ -104,13 +111,19 @@ __device__ inline bool block_peer_allreduce(const PeerCtx& c, const double* vals
   }
   __threadfence_system();
   __syncthreads();
-  if (threadIdx.x == 0) {
-    for (int p = 0; p < c.world; ++p)
-      peer_store_release(&reinterpret_cast<PeerHeader*>(c.bufs[p])->flags[slot][c.rank], c.epoch);
-    const PeerHeader* own = reinterpret_cast<const PeerHeader*>(c.bufs[c.rank]);
-    bool ok = true;
-    for (int p = 0; ok && p < c.world; ++p) ok = peer_wait_flag(c, &own->flags[slot][p], (2 << 8) | p);
-    s_ok = ok ? 1 : 0;
+  if (threadIdx.x < 32) {
+    // warp 0: the pushes of every thread are ordered before this point (their
+    // system fence and the barrier); each lane releases the flag of peers
+    // lane, lane + 32, ...
+    peer_fence_acq_rel();
+    for (int p = threadIdx.x; p < c.world; p += 32)
+      peer_store_relaxed(&reinterpret_cast<PeerHeader*>(c.bufs[p])->flags[slot][c.rank], c.epoch);
+    if (threadIdx.x == 0) {
+      const PeerHeader* own = reinterpret_cast<const PeerHeader*>(c.bufs[c.rank]);
+      bool ok = true;
+      for (int p = 0; ok && p < c.world; ++p) ok = peer_wait_flag(c, &own->flags[slot][p], (2 << 8) | p);
+      s_ok = ok ? 1 : 0;
+    }
   }
   __syncthreads();
   if (!s_ok) {
