@@ -33,7 +33,9 @@ time.  1.0 = every op at its roofline on one B200; N GPUs at perfect
 efficiency give N times the one-GPU value.  The 3xTF32 ceiling is a third of
 cuBLAS's TF32 rate on an 8192^3 GEMM, measured by this script on the same
 GPU just before timing (`peaks`).  `per_op` gives each op's time, GB/s or
-TFLOP/s of the global problem and fraction of the N-GPU roofline.
+TFLOP/s of the global problem and fraction of the N-GPU roofline, from a
+second pass of K steps with an event pair around every op (the step time
+comes from a pass with no events between the ops).
 
 L2: every op's input is larger than the 126 MB L2 or, between two launches of
 one op, the step moves gigabytes through other buffers; no flush is needed
@@ -873,14 +875,29 @@ def _main(sink) -> int:
             fn()
     torch.cuda.synchronize(device)
 
+    # the step time: K steps with nothing but the ops (and flushes) between
+    # one pair of events; then the per-op split in a second pass of K steps
+    # with an event pair around every op (events between kernels are
+    # commands of their own on the stream, so they stay out of the step time)
     clocks = ClockSampler(local_rank)
-    ev = {n: [] for n, *_ in runners}
     barrier()
     torch.cuda.synchronize(device)
     clocks.mark(0)
     t_start = torch.cuda.Event(enable_timing=True)
     t_end = torch.cuda.Event(enable_timing=True)
     t_start.record(stream)
+    for _ in range(a.steps):
+        for _, _, _, fn, _ in runners:
+            if flush_buf is not None:
+                flush_buf.fill_(1.0)
+            fn()
+    t_end.record(stream)
+    torch.cuda.synchronize(device)
+    clocks.mark(1)
+    barrier()
+    total_ms = t_start.elapsed_time(t_end)
+    ev = {n: [] for n, *_ in runners}
+    torch.cuda.synchronize(device)
     for _ in range(a.steps):
         for n, _, _, fn, _ in runners:
             if flush_buf is not None:
@@ -891,11 +908,8 @@ def _main(sink) -> int:
             fn()
             e1.record(stream)
             ev[n].append((e0, e1))
-    t_end.record(stream)
     torch.cuda.synchronize(device)
-    clocks.mark(1)
     barrier()
-    total_ms = t_start.elapsed_time(t_end)
     per_op_ms = {n: sum(e0.elapsed_time(e1) for e0, e1 in ev[n]) / a.steps for n in ev}
     if world > 1:
         t = torch.tensor([total_ms] + [per_op_ms[n] for n in ev], device=device, dtype=torch.float64)
@@ -1037,6 +1051,7 @@ def _main(sink) -> int:
         "higher_is_better": True, "scaling": "strong", "vs_baseline": None, "dtype": "f32",
         "data": "synthetic (seeded, generated on device)", "config": config,
         "roofline": roof, "cpu_baseline": cpu, "e2e": e2e, "clocks": clk,
+        # kernels of ours in the timed step loop (the per-op pass after it runs as many again)
         "gpu_launches": a.steps * sum(launches(n, world, comm, ins) for n, _, ins, _, _ in runners),
         "peaks": peaks,
         "aggregate": {"hbm_ops_gbs": round(hbm_bytes / (hbm_ms * 1e-3) / 1e9, 1) if hbm_ms else None,
