@@ -21,9 +21,10 @@ Multi-GPU is strong scaling: the global problem stays fixed and rank r holds
 and processes only its shard of each op's input (kbb200.workloads.SHARD_DIMS:
 rows, batch items, vector slices, GEMM rows or K slices).  MSE, Frobenius,
 BatchNorm and split-K GEMM add their one exchange between a local partial
-and a local finish (kbb200.dist): the library's peer-memory all-reduce kernel
-where it is faster (2 ranks; payloads <= 64 B beyond), NCCL otherwise;
-`--collective nccl` forces NCCL.  Step times are the max over ranks.
+and a local finish (kbb200.dist): over the library's peer memory — fused into
+the partial kernel for MSE, Frobenius and BatchNorm, the peer all-reduce
+kernel (with the split fold) for split-K — or with `--collective nccl` over
+NCCL.  Step times are the max over ranks.
 
 `value` is roofline-weighted throughput in units of one B200 roofline: the
 sum over the step's ops of the op's one-GPU roofline time (algorithmic bytes

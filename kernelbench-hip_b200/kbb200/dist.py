@@ -19,10 +19,9 @@ B200s; gloo on CPU) or, given `comm=PeerComm(...)` (kbb200.p2p), the
 library's own all-reduce kernel over peer memory; for split-K that kernel
 also performs the rank's own K-split reduction, so local finish and
 cross-GPU sum are one launch.  The peer kernel pushes each rank's payload to
-every peer, so it wins where the exchange is latency-bound: it is used on 2
-ranks for every payload and on more ranks for payloads of at most
-PEER_MAX_BYTES; larger exchanges on more ranks go to NCCL even when a
-PeerComm is given (see peer_path).  The per-shard kernels are injectable
+every peer; it serves every exchange that fits the communicator's slot
+(measured faster than or equal to NCCL from 8 B to 256 KiB on 2 and 8
+ranks), and NCCL takes larger ones (see peer_path).  The per-shard kernels are injectable
 (`kernels=`) so the composition can be tested with CPU implementations on a
 gloo process group; by default they are the CUDA kernels of kbb200.ops.
 """
@@ -58,12 +57,15 @@ def shard(t: torch.Tensor, rank: int, world: int, dim: int = 0) -> torch.Tensor:
     return t.narrow(dim, lo, hi - lo)
 
 
-# Measured on B200s (µs per call, peer kernel vs NCCL all_reduce, NVLS off):
-# 2 ranks 10.5-15.1 vs 18.8-31.5 from 8 B to 2 KiB and 17.6 vs 18.8 at
-# 256 KiB; 4 ranks 14.9 / 15.3 vs 19.9 / 19.0 at 8 / 16 B, but 21.5 vs 17.7
-# at 2 KiB and 30.7 vs 19.5 at 256 KiB (every rank's pushes grow with the
-# world size, NCCL's ring traffic does not).
-PEER_MAX_BYTES = 64
+# Measured on B200s (µs per call, peer kernel vs NCCL all_reduce, NVLS off,
+# bench.py --exchange-sweep), after the peer kernel raised its flags with one
+# fence per lane and parallel relaxed stores: 2 ranks 12.7 / 10.7 / 12.7 /
+# 16.8 vs 17.3 / 17.3 / 19.1 / 40.9 for 8 B / 16 B / 2 KiB / 256 KiB; 8 ranks
+# 14.1 / 14.2 / 17.2 / 27.6 vs 20.3 / 20.4 / 26.3 / 28.1, and the split-K
+# fold + all-reduce in one kernel 32.9 against 59.3 for a local reduction +
+# NCCL.  (With one release store per peer, one after another, the kernel
+# had lost to NCCL from 2 KiB up on 4 ranks: 21.5 vs 17.7 and 30.7 vs 19.5.)
+# So the peer kernel serves every payload that fits its slot.
 # The fused sharded kernels (one CTA pushes this rank's fold to every peer at
 # the end of the partial pass) serve exchanges up to this size on any world
 # size: BatchNorm's 16 C + 8 bytes for C <= 1024.  The push is a few KiB per
@@ -77,8 +79,7 @@ def peer_path(comm, nbytes: int) -> bool:
     beyond the communicator's slot (comm.payload_bytes), which NCCL handles
     instead.  Every rank passes the same nbytes and world size, so all ranks
     take the same path and the collective order stays identical."""
-    return (comm is not None and nbytes <= comm.payload_bytes
-            and (comm.world <= 2 or nbytes <= PEER_MAX_BYTES))
+    return comm is not None and nbytes <= comm.payload_bytes
 
 
 def _fused(comm, nbytes: int) -> bool:
@@ -156,9 +157,9 @@ def matmul_splitk(a: torch.Tensor, b: torch.Tensor, out=None, group=None, kernel
     """C = A @ B with K sharded: rank r holds A[:, K_r] and B[K_r, :].  Each
     rank computes its partial C (split-K across its own SMs as well), then one
     all_reduce sums the partials; every rank ends with the full C.  With a
-    PeerComm on 2 ranks (or a C of at most PEER_MAX_BYTES) the rank's K-split
-    tiles go straight into the peer all-reduce kernel, which sums them (split
-    order) and then across ranks (rank order)."""
+    PeerComm whose slot holds C, the rank's K-split tiles go straight into
+    the peer all-reduce kernel, which sums them (split order) and then
+    across ranks (rank order)."""
     k = kernels or _default_kernels()
     if peer_path(comm, a.shape[0] * b.shape[1] * 4):
         parts, splits = k.matmul_splitk_partials(a, b)

@@ -152,16 +152,16 @@ def test_shard_range_partitions_exactly():
 
 
 def test_peer_path_routing():
-    """The peer all-reduce serves every payload on 2 ranks and only small
-    ones (latency-bound) on more ranks; without a PeerComm it is never used."""
+    """The peer all-reduce serves every payload that fits the communicator's
+    slot, on any world size; without a PeerComm it is never used."""
     from types import SimpleNamespace
 
-    from kbb200.dist import PEER_MAX_BYTES, peer_path
+    from kbb200.dist import peer_path
 
     two, four, eight = (SimpleNamespace(world=w, payload_bytes=1 << 20) for w in (2, 4, 8))
     assert peer_path(two, 8) and peer_path(two, 256 * 1024)
-    assert peer_path(four, 16) and peer_path(eight, PEER_MAX_BYTES)
-    assert not peer_path(four, PEER_MAX_BYTES + 1) and not peer_path(eight, 256 * 1024)
+    assert peer_path(four, 16) and peer_path(eight, 2056) and peer_path(eight, 256 * 1024)
+    assert peer_path(eight, 1 << 20) and not peer_path(eight, (1 << 20) + 1)
     assert not peer_path(None, 8)
     # an exchange larger than the communicator's slot goes to NCCL, on any world size
     small = SimpleNamespace(world=2, payload_bytes=4096)
