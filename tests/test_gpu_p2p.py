@@ -184,3 +184,30 @@ def test_allreduce_many_ranks_rank_ordered(world, cuda_device):
         assert torch.equal(out, want)
     finally:
         em.close()
+
+
+@pytest.mark.parametrize("world", [4, 8])
+def test_splitk_fold_many_ranks(world, cuda_device):
+    """The fused split-K form as rank 0 of 4 and 8 ranks: its own K-split
+    tiles summed in split order, then every rank's part in rank order."""
+    em = Emulated(cuda_device, payload_bytes=1 << 18, world=world)
+    try:
+        n, splits = 65536, 5  # a 256 x 256 C, the split-K benchmark's exchange
+        parts = torch.randn(splits, n, device=cuda_device)
+        peers = [torch.randn(n, device=cuda_device) for _ in range(1, world)]
+        for p, t in enumerate(peers, start=1):
+            em.set_peer(1, t, peer=p)
+        out = torch.empty(n, device=cuda_device)
+        em.check("splitk", em.LIB.kb_p2p_splitk_allreduce_f32(em.bufs.data_ptr(), 0, world, em.buf_bytes,
+                                                              parts.data_ptr(), splits, out.data_ptr(), n, 1,
+                                                              2_000_000_000, _stream()))
+        assert _fault() == 0
+        local = parts[0].clone()
+        for z in range(1, splits):
+            local = local + parts[z]
+        want = torch.zeros_like(local) + local
+        for t in peers:
+            want = want + t
+        assert torch.equal(out, want)
+    finally:
+        em.close()
