@@ -32,8 +32,12 @@ at the measured copy bandwidth; for the tensor-core GEMMs the useful FLOPs
 at the 3xTF32 ceiling when that takes longer) divided by the measured step
 time.  1.0 = every op at its roofline on one B200; N GPUs at perfect
 efficiency give N times the one-GPU value.  The 3xTF32 ceiling is a third of
-cuBLAS's TF32 rate on an 8192^3 GEMM, measured by this script on the same
-GPU just before timing (`peaks`).  `per_op` gives each op's time, GB/s or
+cuBLAS's TF32 burst rate on an 8192^3 GEMM (the highest this probe measured
+on the pool; the live probe of the same GPU just before timing is recorded in
+`peaks`).  When the op with the largest share of the step is a GEMM, the
+`roofline` record divides by the sustained ceiling (the burst one times the
+live sustained / burst TF32 ratio: the GEMM runs inside a long, power-capped
+step) and keeps the burst fraction beside it.  `per_op` gives each op's time, GB/s or
 TFLOP/s of the global problem and fraction of the N-GPU roofline, from a
 second pass of K steps with an event pair around every op (the step time
 comes from a pass with no events between the ops).
@@ -147,15 +151,20 @@ def ncu_traffic(name: str) -> float | None:
 def load_peaks() -> dict:
     if PEAKS_FILE.exists():
         p = json.loads(PEAKS_FILE.read_text())
-        return {"hbm_gbs": float(p["hbm_gbs"]), "bf16_tflops": float(p["bf16_tflops"]),
-                "source": "measured (MEASURED_PEAKS.json)"}
+        out = {"hbm_gbs": float(p["hbm_gbs"]), "bf16_tflops": float(p["bf16_tflops"]),
+               "source": "measured (MEASURED_PEAKS.json)"}
+        if p.get("bf16_tflops_sustained"):
+            out["bf16_tflops_sustained"] = float(p["bf16_tflops_sustained"])
+        return out
     return {"hbm_gbs": FALLBACK_HBM_GBS, "bf16_tflops": FALLBACK_BF16_TFLOPS, "source": "fallback"}
 
 
-def measure_tf32_tflops(device, n: int = 8192, reps: int = 10) -> float:
-    """cuBLAS TF32 dense rate on this GPU (torch.matmul, allow_tf32, n^3,
-    best of `reps`, CUDA events): the tensor-core rate 3xTF32 divides by
-    three.  Runs before any timed region."""
+def measure_tf32_tflops(device, n: int = 8192, reps: int = 10, sustain_s: float = 3.0) -> dict:
+    """cuBLAS TF32 dense rate on this GPU (torch.matmul, allow_tf32, n^3):
+    the tensor-core rate 3xTF32 divides by three.  `burst`: best of `reps`
+    single calls (CUDA events); `sustained`: back-to-back calls for about
+    `sustain_s` seconds, timed as one block, so the power cap has settled the
+    clock as it does inside a long step.  Runs before any timed region."""
     prev = torch.backends.cuda.matmul.allow_tf32
     torch.backends.cuda.matmul.allow_tf32 = True
     try:
@@ -173,20 +182,51 @@ def measure_tf32_tflops(device, n: int = 8192, reps: int = 10) -> float:
             e1.record()
             torch.cuda.synchronize(device)
             best = min(best, e0.elapsed_time(e1))
+        out = {"burst": 2.0 * n ** 3 / (best * 1e-3) / 1e12}
+        if sustain_s > 0:
+            calls = max(4, int(sustain_s / (best * 1e-3)))
+            e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+            e0.record()
+            for _ in range(calls):
+                torch.matmul(a, b, out=c)
+            e1.record()
+            torch.cuda.synchronize(device)
+            out["sustained"] = 2.0 * n ** 3 * calls / (e0.elapsed_time(e1) * 1e-3) / 1e12
+            out["sustained_calls"] = calls
         del a, b, c
-        return 2.0 * n ** 3 / (best * 1e-3) / 1e12
+        return out
     finally:
         torch.backends.cuda.matmul.allow_tf32 = prev
 
 
-def _tensor_peak(peaks: dict, live_tf32: float | None) -> None:
-    """Record the 3xTF32 ceiling both arms use, and this run's live probe."""
+def _tensor_peak(peaks: dict, live: dict | None) -> None:
+    """Record the 3xTF32 ceiling both arms use, and this run's live probe.
+
+    `tensor_tflops` (burst) is the unit of `value` and of the per-op
+    fractions.  `tensor_tflops_sustained` is the same ceiling under the power
+    cap, the denominator for a GEMM timed inside the long step: the burst
+    ceiling times this box's live sustained / burst TF32 ratio (or, without a
+    live probe, the pool's measured bf16 sustained / burst ratio)."""
     peaks["tf32_tflops"] = TF32_CEILING_TFLOPS
     peaks["tensor_tflops"] = round(TF32_CEILING_TFLOPS / 3.0, 2)
     peaks["tensor_source"] = ("3xTF32 ceiling = a third of cuBLAS TF32 8192^3, highest burst measured on this "
                               "pool by measure_tf32_tflops")
-    if live_tf32 is not None:
-        peaks["tf32_tflops_live"] = round(live_tf32, 1)
+    ratio, how = None, None
+    if live is not None:
+        peaks["tf32_tflops_live"] = round(live["burst"], 1)
+        if live.get("sustained"):
+            peaks["tf32_tflops_live_sustained"] = round(live["sustained"], 1)
+            ratio = live["sustained"] / live["burst"]
+            how = (f"live cuBLAS TF32 sustained / burst on this GPU ({live['sustained']:.1f} / "
+                   f"{live['burst']:.1f}, {live['sustained_calls']} back-to-back 8192^3 calls)")
+    if ratio is None and peaks.get("bf16_tflops_sustained"):
+        ratio = peaks["bf16_tflops_sustained"] / peaks["bf16_tflops"]
+        how = (f"MEASURED_PEAKS.json bf16 sustained / burst ({peaks['bf16_tflops_sustained']} / "
+               f"{peaks['bf16_tflops']})")
+    if ratio is not None:
+        ratio = min(ratio, 1.0)
+        peaks["tensor_tflops_sustained"] = round(peaks["tensor_tflops"] * ratio, 2)
+        peaks["tensor_sustained_source"] = f"3xTF32 burst ceiling x {ratio:.4f} = {how}"
 
 
 def host_llc_bytes() -> tuple[int, str]:
@@ -950,8 +990,13 @@ def _main(sink) -> int:
     dom_ms = per_op_ms[dom_name]
     if roofline_bound(dom_w, hbm, tens) == "tensor":
         achieved = dom_w.flops / (dom_ms * 1e-3) / 1e12
-        roof = {"bound": "tensor", "unit": "TFLOP/s", "peak": round(tens * world, 2),
-                "peak_source": peaks["tensor_source"] + (f" x {world} GPUs" if world > 1 else ""),
+        # a GEMM timed inside the long step runs under the power cap: its
+        # denominator is the sustained ceiling; the burst one stays beside it
+        sus = peaks.get("tensor_tflops_sustained")
+        roof = {"bound": "tensor", "unit": "TFLOP/s", "peak": round((sus or tens) * world, 2),
+                "peak_source": (peaks["tensor_sustained_source"] if sus else peaks["tensor_source"])
+                + (f" x {world} GPUs" if world > 1 else ""),
+                "peak_burst": round(tens * world, 2), "frac_vs_burst": round(achieved / (tens * world), 4),
                 "bf16_measured_tflops": peaks["bf16_tflops"]}
     else:
         achieved = dom_w.algo_bytes / (dom_ms * 1e-3) / 1e9

@@ -59,13 +59,14 @@ __device__ __forceinline__ MaxSum ms_combine(MaxSum a, MaxSum b) {
   const float M = fmaxf(a.m, b.m);
   return {M, a.s * ms_rescale(a.m, M) + b.s * ms_rescale(b.m, M)};
 }
+// Warp combine in three steps: a max butterfly, one rescale of each lane's
+// sum to the warp max, a sum butterfly.  One exponential per lane instead of
+// two per butterfly round: with every warp of a CTA combining at once, the
+// per-round exponentials kept the special-function pipe busy for hundreds
+// of cycles per row.  Both butterflies leave every lane with the same bits.
 __device__ __forceinline__ MaxSum warp_ms(MaxSum v) {
-#pragma unroll
-  for (int o = 16; o > 0; o >>= 1) {
-    const MaxSum u{__shfl_xor_sync(0xffffffffu, v.m, o), __shfl_xor_sync(0xffffffffu, v.s, o)};
-    v = ms_combine(v, u);
-  }
-  return v;
+  const float M = warp_max(v.m);
+  return {M, warp_sum(v.s * ms_rescale(v.m, M))};
 }
 // Block-wide combine; `red` holds >= 64 floats.
 template <int NT>
@@ -387,11 +388,49 @@ __device__ __forceinline__ void bulk_load(uint32_t dst, const void* src, uint32_
       : "memory");
 }
 
+// Moves this thread's vectors k0 .. k1-1 (k0, k1 even) of a row segment from
+// shared memory into registers; ok[k] tells whether vector k lies inside the
+// segment.  With PAIRED slots, lane l owns float4s 2l and 2l+1 of each pair
+// group, so reading "the even float4 of every lane" is a 32-byte-strided
+// access: each quarter-warp of a 128-bit shared load touches only 16 of the
+// 32 banks twice and needs two wavefronts.  Lanes with bit 2 set therefore
+// read the odd float4 of their pair first: every quarter-warp then covers all
+// 32 banks once per load, and the pair is put back in order in registers, so
+// the values (and every result computed from them) are unchanged.
+template <bool PAIRED, int VPT>
+__device__ __forceinline__ void read_segment(float4 (&v)[VPT], bool (&ok)[VPT], const float4* buf, int k0,
+                                             int k1, int lane, int stride, int seg4, bool live) {
+  const float4 zero = make_float4(0.f, 0.f, 0.f, 0.f);
+  if constexpr (PAIRED) {
+    const int sw = (lane >> 2) & 1;
+#pragma unroll
+    for (int k = 0; k < VPT; k += 2) {
+      if (k < k0 || k >= k1) continue;
+      const int64_t j0 = vec_slot<true>(k, lane, stride);  // even float4 of the pair
+      const int64_t ja = j0 + sw, jb = j0 + (sw ^ 1);
+      const float4 fa = (live && ja < seg4) ? buf[ja] : zero;
+      const float4 fb = (live && jb < seg4) ? buf[jb] : zero;
+      v[k] = sw ? fb : fa;
+      v[k + 1] = sw ? fa : fb;
+      ok[k] = j0 < seg4;
+      ok[k + 1] = j0 + 1 < seg4;
+    }
+  } else {
+#pragma unroll
+    for (int k = 0; k < VPT; ++k) {
+      if (k < k0 || k >= k1) continue;
+      const int64_t j = vec_slot<false>(k, lane, stride);
+      ok[k] = j < seg4;
+      v[k] = (live && ok[k]) ? buf[j] : zero;
+    }
+  }
+}
+
 template <RowOp OP, int NT, int VPT, int CL, int DEPTH, bool PAIRED>
 __global__ void __launch_bounds__(NT) row_persist_kernel(RowArgs a) {
   extern __shared__ float4 seg_buf[];  // DEPTH segment buffers
   __shared__ float red[64];
-  __shared__ float slots[4];
+  __shared__ float slots[8];  // two sets, alternating by row
   __shared__ __align__(8) uint64_t bars[DEPTH];
   int rank = 0;
   if constexpr (CL > 1) rank = (int)cg::this_cluster().block_rank();
@@ -419,18 +458,16 @@ __global__ void __launch_bounds__(NT) row_persist_kernel(RowArgs a) {
   ClusterReducer<NT, CL> r{red, slots};
   int64_t i = 0;
   for (int64_t row = cluster_id; row < a.rows; row += nclusters, ++i) {
+    // alternate slot sets: a peer may still read this CTA's set of the
+    // previous row until it reaches this row's cluster barrier
+    r.slots = slots + 4 * (int)(i & 1);
     const int slot = (int)(i % DEPTH);
     const uint32_t parity = (uint32_t)((i / DEPTH) & 1);
     const float4* buf = seg_buf + (size_t)slot * seg4;
     bool got = alive ? wait_bounded(smem_addr(&bars[slot]), parity) : true;
     float4 v[VPT];
     bool ok[VPT];
-#pragma unroll
-    for (int k = 0; k < VPT; ++k) {
-      const int64_t j = vec_slot<PAIRED>(k, threadIdx.x, NT);
-      ok[k] = j < seg4;
-      v[k] = (ok[k] && alive && got) ? buf[j] : make_float4(0.f, 0.f, 0.f, 0.f);
-    }
+    read_segment<PAIRED>(v, ok, buf, 0, VPT, threadIdx.x, NT, seg4, alive && got);
     // everyone has read the buffer (and agrees whether the copy landed)
     got = __syncthreads_and(got) != 0;
     if (!got && alive) {
@@ -461,9 +498,10 @@ template <RowOp OP, int NT, int VPT, int CL, bool PAIRED>
 __global__ void __launch_bounds__(NT) row_persist_halves_kernel(RowArgs a) {
   extern __shared__ float4 seg_buf[];  // one row segment: [first half | second half]
   __shared__ float red[64];
-  __shared__ float slots[4];
+  __shared__ float slots[8];  // two sets, alternating by row
   __shared__ __align__(8) uint64_t bars[2];
   constexpr int H = VPT / 2;
+  static_assert(!PAIRED || H % 2 == 0, "pairs must not straddle the two halves");
   int rank = 0;
   if constexpr (CL > 1) rank = (int)cg::this_cluster().block_rank();
   const int64_t cluster_id = blockIdx.x / CL, nclusters = gridDim.x / CL;
@@ -489,6 +527,9 @@ __global__ void __launch_bounds__(NT) row_persist_halves_kernel(RowArgs a) {
   ClusterReducer<NT, CL> r{red, slots};
   int64_t i = 0;
   for (int64_t row = cluster_id; row < a.rows; row += nclusters, ++i) {
+    // alternate slot sets: a peer may still read this CTA's set of the
+    // previous row until it reaches this row's cluster barrier
+    r.slots = slots + 4 * (int)(i & 1);
     const uint32_t parity = (uint32_t)(i & 1);
     const int64_t next = row + nclusters;
     const float* nsrc = xseg + next * (int64_t)a.cols;
@@ -496,23 +537,13 @@ __global__ void __launch_bounds__(NT) row_persist_halves_kernel(RowArgs a) {
     bool ok[VPT];
     // first half: read out, then refill it with the next row's first half
     bool got = alive ? wait_bounded(smem_addr(&bars[0]), parity) : true;
-#pragma unroll
-    for (int k = 0; k < H; ++k) {
-      const int64_t j = vec_slot<PAIRED>(k, threadIdx.x, NT);
-      ok[k] = j < seg4;
-      v[k] = (ok[k] && alive && got) ? seg_buf[j] : make_float4(0.f, 0.f, 0.f, 0.f);
-    }
+    read_segment<PAIRED>(v, ok, seg_buf, 0, H, threadIdx.x, NT, seg4, alive && got);
     bool all = __syncthreads_and(got) != 0;
     if (threadIdx.x == 0 && alive && all && next < a.rows)
       bulk_load(smem_addr(seg_buf), nsrc, (uint32_t)half4 * 16u, smem_addr(&bars[0]));
     // second half
     got = (alive && all && rest4 > 0) ? wait_bounded(smem_addr(&bars[1]), parity) : true;
-#pragma unroll
-    for (int k = H; k < VPT; ++k) {
-      const int64_t j = vec_slot<PAIRED>(k, threadIdx.x, NT);
-      ok[k] = j < seg4;
-      v[k] = (ok[k] && alive && all && got) ? seg_buf[j] : make_float4(0.f, 0.f, 0.f, 0.f);
-    }
+    read_segment<PAIRED>(v, ok, seg_buf, H, VPT, threadIdx.x, NT, seg4, alive && all && got);
     all = (__syncthreads_and(got) != 0) && all;
     if (threadIdx.x == 0 && alive && all && rest4 > 0 && next < a.rows)
       bulk_load(smem_addr(seg_buf + half4), nsrc + (int64_t)half4 * 4, (uint32_t)rest4 * 16u,

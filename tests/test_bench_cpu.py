@@ -67,3 +67,26 @@ def test_value_units_scale_with_the_gpu_count():
     roof = sum(roofline_seconds(WORKLOADS[n], hbm, tens) for n in FAMILIES["northstar"])
     assert len(FAMILIES["northstar"]) == 19
     assert 0.015 < roof < 0.02  # ~17.7 ms of one-B200 roofline time per step
+
+
+def test_tensor_peak_sustained_denominator():
+    """The in-step GEMM denominator is the burst 3xTF32 ceiling scaled by the
+    live sustained / burst TF32 ratio, else by the pool's bf16 ratio, and is
+    never above the burst ceiling."""
+    sys.path.insert(0, str(REPO))
+    import bench
+
+    peaks = {"hbm_gbs": 6448.7, "bf16_tflops": 1676.2, "bf16_tflops_sustained": 1396.9, "source": "test"}
+    bench._tensor_peak(peaks, {"burst": 760.0, "sustained": 608.0, "sustained_calls": 2000})
+    burst = bench.TF32_CEILING_TFLOPS / 3.0
+    assert peaks["tensor_tflops"] == round(burst, 2)
+    assert peaks["tensor_tflops_sustained"] == round(round(burst, 2) * 0.8, 2)
+    assert "live cuBLAS TF32" in peaks["tensor_sustained_source"]
+
+    peaks = {"hbm_gbs": 6448.7, "bf16_tflops": 1676.2, "bf16_tflops_sustained": 1396.9, "source": "test"}
+    bench._tensor_peak(peaks, None)
+    assert peaks["tensor_tflops_sustained"] == round(round(burst, 2) * 1396.9 / 1676.2, 2)
+
+    peaks = {"hbm_gbs": 6448.7, "bf16_tflops": 1676.2, "source": "test"}
+    bench._tensor_peak(peaks, {"burst": 700.0, "sustained": 720.0, "sustained_calls": 10})
+    assert peaks["tensor_tflops_sustained"] == peaks["tensor_tflops"]

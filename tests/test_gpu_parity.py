@@ -123,6 +123,41 @@ def test_row_ops_all_paths(op, cols, cuda_device):
     assert_close(got.cpu().numpy(), want, 1e-5, f"{op} cols={cols}")
 
 
+@pytest.mark.parametrize("cols", [8192, 32768, 65536, 131072])
+@pytest.mark.parametrize("op", ["layer_norm", "rms_norm", "softmax", "log_softmax"])
+def test_row_ops_many_rows(op, cols, cuda_device):
+    """Enough rows that every persistent CTA (or 2/4-CTA cluster) walks
+    several rows: the prefetch ring, the DSMEM slot sets that alternate by row
+    and the per-row merges all repeat.  LayerNorm rows sit on an offset of
+    1000 with spread 2: a one-pass E[x^2] - mean^2 would lose percent-level
+    accuracy in the variance there (x^2 ~ 1e6 in fp32), while the per-thread
+    two-pass statistics and their pairwise merge stay near the fp32 rounding
+    of a mean of 1000 (3e-5, i.e. ~1.5e-5 of the output), inside the 2e-4
+    tolerance."""
+    from kbb200 import ops as K
+
+    rows = 600 if cols <= 65536 else 400
+    g = torch.Generator().manual_seed(cols + 7)
+    x = torch.randn(rows, cols, generator=g) * 2
+    xd = x.to(cuda_device)
+    tol = 1e-5
+    if op == "layer_norm":
+        x = x + 1000.0
+        xd = x.to(cuda_device)
+        w = 1 + 0.1 * torch.randn(cols, generator=g)
+        b = 0.1 * torch.randn(cols, generator=g)
+        got = K.layer_norm(xd, w.to(cuda_device), b.to(cuda_device))
+        want = O.layer_norm(x.numpy(), w.numpy(), b.numpy())
+        tol = 2e-4
+    elif op == "rms_norm":
+        got, want = K.rms_norm(xd), O.rms_norm(x.numpy())
+    elif op == "softmax":
+        got, want = K.softmax(xd), O.softmax(x.numpy())
+    else:
+        got, want = K.log_softmax(xd), O.log_softmax(x.numpy())
+    assert_close(got.cpu().numpy(), want, tol, f"{op} rows={rows} cols={cols}")
+
+
 @pytest.mark.parametrize("op", ["layer_norm", "softmax"])
 def test_row_ops_unaligned_and_no_affine(op, cuda_device):
     from kbb200 import ops as K
