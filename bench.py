@@ -815,6 +815,9 @@ def _main(sink) -> int:
     ap.add_argument("--collective", choices=("p2p", "nccl"), default="p2p",
                     help="cross-GPU sum of the sharded ops: the library's peer-memory kernel or NCCL")
     ap.add_argument("--frac", type=float, default=0.25, help="input fraction for --profile-op")
+    ap.add_argument("--tf32-sustain-s", type=float, default=3.0,
+                    help="seconds of back-to-back cuBLAS TF32 calls for the sustained tensor ceiling "
+                         "(0: none, the pool's bf16 sustained / burst ratio instead; for launch lists)")
     a = ap.parse_args()
     if a.profile_op:
         return profile_op(a.profile_op, a.frac)
@@ -878,7 +881,7 @@ def _main(sink) -> int:
             from kbb200.p2p import PeerComm
 
             comm = PeerComm(payload_bytes=1 << 20, timeout_s=10.0, device=device)
-    _tensor_peak(peaks, measure_tf32_tflops(device))
+    _tensor_peak(peaks, measure_tf32_tflops(device, sustain_s=a.tf32_sustain_s))
 
     runners = []
     shared: dict[str, list] = {}
