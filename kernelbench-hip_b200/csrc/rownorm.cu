@@ -200,7 +200,7 @@ __device__ __forceinline__ float ex2_ftz(float x) {
   return y;
 }
 
-template <RowOp OP, int VPT, bool PAIRED = false, class R>
+template <RowOp OP, int VPT, bool PAIRED = false, bool EMIT = true, class R>
 __device__ __forceinline__ void row_math(float4 (&v)[VPT], const bool (&ok)[VPT],
                                          const RowArgs& a, float4* yrow, int64_t col4_base,
                                          int stride, int lane, const R& red, bool store = true) {
@@ -306,7 +306,7 @@ __device__ __forceinline__ void row_math(float4 (&v)[VPT], const bool (&ok)[VPT]
         v[k] = make_float4((v[k].x - m) - lse, (v[k].y - m) - lse, (v[k].z - m) - lse, (v[k].w - m) - lse);
     }
   }
-  if (store) store_row<VPT, PAIRED>(yrow, v, ok, lane, stride);
+  if (EMIT && store) store_row<VPT, PAIRED>(yrow, v, ok, lane, stride);
 }
 
 // One CTA (or one CL-CTA cluster) per row; NT threads x VPT float4 each.
@@ -484,6 +484,49 @@ __global__ void __launch_bounds__(NT) row_persist_kernel(RowArgs a) {
     asm volatile("barrier.cluster.arrive.relaxed.aligned;\n\tbarrier.cluster.wait.aligned;" ::: "memory");
 }
 
+// Row results through shared memory and bulk (TMA) stores: pair group c of
+// the paired layout (float4 slots c*2*NT .. c*2*NT + 2*NT - 1 of the segment,
+// 32 KB for NT = 1024) is written into one of two staging buffers and leaves
+// as one cp.async.bulk store issued by thread 0.  The registers are free as
+// soon as the shared-memory writes are done, and the stores no longer queue
+// in the SM's load/store unit behind the next row's read-out.  Thread 0 owns
+// every bulk group, so its wait_group.read 1 before a buffer is reused (the
+// store two groups back read that buffer) covers them all.  Lanes with bit 2
+// set write the odd float4 of their pair first (no bank conflicts).
+__device__ __forceinline__ void bulk_store_wait_read1() {
+  asm volatile("cp.async.bulk.wait_group.read 1;" ::: "memory");
+}
+__device__ __forceinline__ void bulk_store_wait_all() {
+  asm volatile("cp.async.bulk.wait_group 0;" ::: "memory");
+}
+template <int NT, int VPT>
+__device__ __forceinline__ void staged_store_row(float4* ys, const float4 (&v)[VPT], int seg4, float4* stage,
+                                                 bool live) {
+  const int lane = threadIdx.x;
+  const int sw = (lane >> 2) & 1;
+#pragma unroll
+  for (int c = 0; c < VPT / 2; ++c) {
+    const int g0 = c * 2 * NT;
+    if (g0 >= seg4) break;  // uniform over the CTA
+    float4* buf = stage + (c & 1) * 2 * NT;
+    if (threadIdx.x == 0) bulk_store_wait_read1();
+    __syncthreads();
+    if (live) {
+      buf[2 * lane + sw] = sw ? v[2 * c + 1] : v[2 * c];
+      buf[2 * lane + (sw ^ 1)] = sw ? v[2 * c] : v[2 * c + 1];
+      asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
+    }
+    __syncthreads();
+    if (threadIdx.x == 0 && live) {
+      const uint32_t bytes = (uint32_t)min(2 * NT, seg4 - g0) * 16u;
+      asm volatile("cp.async.bulk.global.shared::cta.bulk_group [%0], [%1], %2;" ::"l"(ys + g0),
+                   "r"(smem_addr(buf)), "r"(bytes)
+                   : "memory");
+      asm volatile("cp.async.bulk.commit_group;" ::: "memory");
+    }
+  }
+}
+
 // The same persistent walk with the prefetch in two halves.  With one
 // buffer for the whole row segment, the next row's copy can start only after
 // every thread has moved the whole current row into registers, so each SM's
@@ -494,9 +537,12 @@ __global__ void __launch_bounds__(NT) row_persist_kernel(RowArgs a) {
 // first half is already being fetched while the second half is read out.
 // Each thread's first VPT/2 vectors lie in the first half (vec_slot), so the
 // register layout and the math are unchanged.
-template <RowOp OP, int NT, int VPT, int CL, bool PAIRED>
+template <RowOp OP, int NT, int VPT, int CL, bool PAIRED, bool TST>
 __global__ void __launch_bounds__(NT) row_persist_halves_kernel(RowArgs a) {
-  extern __shared__ float4 seg_buf[];  // one row segment: [first half | second half]
+  // one row segment: [first half | second half], then with TST two 2*NT-float4
+  // staging buffers for the bulk result stores
+  extern __shared__ float4 seg_buf[];
+  static_assert(!TST || (PAIRED && CL == 1), "staged stores: paired layout, one CTA per row");
   __shared__ float red[64];
   __shared__ float slots[8];  // two sets, alternating by row
   __shared__ __align__(8) uint64_t bars[2];
@@ -553,16 +599,20 @@ __global__ void __launch_bounds__(NT) row_persist_halves_kernel(RowArgs a) {
       if (threadIdx.x == 0) atomicExch(&g_row_fault, 1);
     }
     float4* ys = reinterpret_cast<float4*>(a.y + row * (int64_t)a.cols) + col4_base;
-    row_math<OP, VPT, PAIRED>(v, ok, a, ys, col4_base, NT, threadIdx.x, r, alive);
+    row_math<OP, VPT, PAIRED, !TST>(v, ok, a, ys, col4_base, NT, threadIdx.x, r, alive);
+    if constexpr (TST) staged_store_row<NT, VPT>(ys, v, seg4, seg_buf + seg4, alive);
+  }
+  if constexpr (TST) {
+    if (threadIdx.x == 0) bulk_store_wait_all();  // stores done before the CTA's shared memory goes
   }
   if constexpr (CL > 1)
     asm volatile("barrier.cluster.arrive.relaxed.aligned;\n\tbarrier.cluster.wait.aligned;" ::: "memory");
 }
 
-template <RowOp OP, int NT, int VPT, int CL, bool PAIRED>
+template <RowOp OP, int NT, int VPT, int CL, bool PAIRED, bool TST>
 cudaError_t launch_halves_impl(const RowArgs& a, cudaStream_t s) {
-  auto kern = row_persist_halves_kernel<OP, NT, VPT, CL, PAIRED>;
-  const int smem = a.cols / CL * 4;
+  auto kern = row_persist_halves_kernel<OP, NT, VPT, CL, PAIRED, TST>;
+  const int smem = a.cols / CL * 4 + (TST ? 2 * 2 * NT * 16 : 0);
   static uint64_t attr_set = 0;
   int dev = 0;
   cudaGetDevice(&dev);
@@ -591,11 +641,11 @@ cudaError_t launch_halves_impl(const RowArgs& a, cudaStream_t s) {
   return cudaLaunchKernelEx(&cfg, kern, a);
 }
 
-template <RowOp OP, int NT, int VPT, int CL>
+template <RowOp OP, int NT, int VPT, int CL, bool TST = false>
 cudaError_t launch_halves(const RowArgs& a, cudaStream_t s) {
   if (aligned32(a.x) && aligned32(a.y) && a.cols % (8 * CL) == 0)
-    return launch_halves_impl<OP, NT, VPT, CL, true>(a, s);
-  return launch_halves_impl<OP, NT, VPT, CL, false>(a, s);
+    return launch_halves_impl<OP, NT, VPT, CL, true, TST>(a, s);
+  return launch_halves_impl<OP, NT, VPT, CL, false, false>(a, s);
 }
 
 template <RowOp OP, int NT, int VPT, int CL, int DEPTH, bool PAIRED>
@@ -766,8 +816,9 @@ int launch_rows(const char* name, const RowArgs& a, cudaStream_t s) {
     e = launch_block<OP, 512, 8, 1>(a, s);
   } else if (c <= 32768) {
     // one persistent 1024-thread CTA per SM: the row in registers, the next
-    // row streaming into shared memory in two halves
-    e = launch_halves<OP, 1024, 8, 1>(a, s);
+    // row streaming into shared memory in two halves, results leaving through
+    // shared memory as bulk stores
+    e = launch_halves<OP, 1024, 8, 1, true>(a, s);
   } else if (c <= 65536 && c % 8 == 0) {
     e = launch_persist<OP, 1024, 8, 2, 1>(a, s);
   } else if (c % 16 == 0) {

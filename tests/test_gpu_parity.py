@@ -289,7 +289,8 @@ def test_batchnorm_shapes_and_running_stats(shape, cuda_device):
     np.testing.assert_allclose(rv.cpu().numpy(), erv, rtol=1e-5, atol=1e-6)
 
 
-@pytest.mark.parametrize("mk", [(1, 1), (3, 7), (17, 1031), (64, 4096), (5, 100003)])
+@pytest.mark.parametrize("mk", [(1, 1), (3, 7), (17, 1031), (64, 4096), (5, 100003), (1, 4096), (7, 4100),
+                                (130, 1 << 16), (4093, 2052)])
 def test_gemv_shapes(mk, cuda_device):
     from kbb200 import ops as K
 
