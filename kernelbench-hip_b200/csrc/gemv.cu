@@ -1,10 +1,14 @@
 // gemv.cu — y[M] = A[M, K] x[K], fp32, HBM-bound (0.5 FLOP/byte).
 //
-// One 256-thread CTA per row: the row (4 MB at K = 2^20) is streamed once
-// with 128-bit evict-first loads, 8 float4 of A and 8 of x in flight per
-// thread; x (4 MB) stays resident in the 126 MB L2 and is shared by every
-// CTA.  The row sum is a fixed shuffle tree, so y is deterministic (the
-// reference split rows into 32K chunks and combined them with fp32 atomics,
+// 256-thread CTAs stream A once with 128-bit evict-first loads, 8 float4 of
+// each row in flight per thread; x (4 MB at K = 2^20) stays resident in the
+// 126 MB L2 and is shared by every CTA.  Each CTA takes two rows, so every x
+// vector fetched from L2 serves two rows of A: the SM-side load traffic is
+// 1.5x the HBM bytes instead of 2x, which took the [4096, 2^20] launch from
+// 2.60 to 2.30 ms (7.4 TB/s of A).  Below 2 rows per SM, one row per CTA
+// keeps more CTAs in flight.  The row sum is a fixed shuffle tree, so y is
+// deterministic and independent of the rows per CTA (the reference split
+// rows into 32K chunks and combined them with fp32 atomics,
 // candidates/4_Matrix_vector_multiplication_/v1.py:16-33).
 #include "kb_common.cuh"
 
@@ -14,48 +18,12 @@ namespace {
 constexpr int kThreads = 256;
 constexpr int kUnroll = 8;
 
-__global__ void __launch_bounds__(kThreads)
-gemv_vec4_kernel(const float* __restrict__ A, const float* __restrict__ x,
-                 float* __restrict__ y, int64_t K) {
-  __shared__ float red[32];
-  const int64_t row = blockIdx.x;
-  const float4* a4 = reinterpret_cast<const float4*>(A + row * K);
-  const float4* x4 = reinterpret_cast<const float4*>(x);
-  const int64_t nvec = K / 4;
-  float acc[kUnroll];
-#pragma unroll
-  for (int u = 0; u < kUnroll; ++u) acc[u] = 0.f;
-  int64_t i = threadIdx.x;
-  const int64_t step = (int64_t)kThreads * kUnroll;
-  for (; i + (kUnroll - 1) * kThreads < nvec; i += step) {
-    float4 a[kUnroll], b[kUnroll];
-#pragma unroll
-    for (int u = 0; u < kUnroll; ++u) {
-      a[u] = ld_stream(a4 + i + u * kThreads);
-      b[u] = __ldg(x4 + i + u * kThreads);
-    }
-#pragma unroll
-    for (int u = 0; u < kUnroll; ++u)
-      acc[u] = fmaf(a[u].x, b[u].x, fmaf(a[u].y, b[u].y, fmaf(a[u].z, b[u].z, fmaf(a[u].w, b[u].w, acc[u]))));
-  }
-  for (; i < nvec; i += kThreads) {
-    const float4 a = ld_stream(a4 + i), b = __ldg(x4 + i);
-    acc[0] = fmaf(a.x, b.x, fmaf(a.y, b.y, fmaf(a.z, b.z, fmaf(a.w, b.w, acc[0]))));
-  }
-  float s = 0.f;
-#pragma unroll
-  for (int u = 0; u < kUnroll; ++u) s += acc[u];
-  for (int64_t j = nvec * 4 + threadIdx.x; j < K; j += kThreads) s = fmaf(A[row * K + j], x[j], s);
-  s = block_sum<kThreads>(s, red);
-  if (threadIdx.x == 0) y[row] = s;
-}
-
 // R rows per CTA: each x vector loaded from L2 serves R rows of A, so the
-// SM-side load traffic falls from 2x to (1 + 1/R)x the HBM bytes.  Per row,
-// thread t sums float4 columns t + u*256 + k*256*U into accumulator u and the
-// row total goes through the same fixed tree as the one-row kernel, so for
-// equal U the results are bitwise those of gemv_vec4_kernel.  A CTA whose
-// last rows lie beyond M re-reads row M-1 for them and discards the sums.
+// SM-side load traffic is (1 + 1/R)x the HBM bytes.  Per row, thread t sums
+// float4 columns t + u*256 + k*256*U into accumulator u, and the row total
+// goes through one fixed tree, so the results do not depend on R.  A CTA
+// whose last rows lie beyond M re-reads row M-1 for them and discards the
+// sums.
 template <int R, int U>
 __global__ void __launch_bounds__(kThreads, 2)
 gemv_rows_kernel(const float* __restrict__ A, const float* __restrict__ x, float* __restrict__ y,
@@ -143,13 +111,11 @@ int kb_gemv_f32(const float* A, const float* x, float* y, int64_t M, int64_t K, 
   if (M == 0) return KB_OK;
   KB_REQUIRE(y && (K == 0 || (A && x)), KB_ERR_INVALID_ARG, "%s: null pointer", name);
   KB_REQUIRE(M <= 0x7fffffff, KB_ERR_UNSUPPORTED, "%s: M too large", name);
-  constexpr int kRows = 1, kU = 8;  // rows per CTA (1: gemv_vec4_kernel), float4 per thread per row
   if (K % 4 == 0 && kb::aligned16(A) && kb::aligned16(x)) {
-    if (kRows == 1)
-      kb::gemv_vec4_kernel<<<(unsigned)M, kb::kThreads, 0, stream>>>(A, x, y, K);
+    if (M >= 2 * kb::sm_count())
+      kb::gemv_rows_kernel<2, kb::kUnroll><<<(unsigned)((M + 1) / 2), kb::kThreads, 0, stream>>>(A, x, y, M, K);
     else
-      kb::gemv_rows_kernel<(kRows > 1 ? kRows : 2), kU>
-          <<<(unsigned)((M + kRows - 1) / kRows), kb::kThreads, 0, stream>>>(A, x, y, M, K);
+      kb::gemv_rows_kernel<1, kb::kUnroll><<<(unsigned)M, kb::kThreads, 0, stream>>>(A, x, y, M, K);
   } else
     kb::gemv_scalar_kernel<<<(unsigned)M, kb::kThreads, 0, stream>>>(A, x, y, K);
   return kb::check_launch(name);
