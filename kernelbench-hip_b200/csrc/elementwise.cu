@@ -72,9 +72,11 @@ struct Vec<4> {
 // One kTile-float tile per CTA, all of a thread's loads issued before any
 // math.  A grid of n / kTile short-lived CTAs streams HBM faster on B200 than a
 // persistent grid-stride loop over the same tiles (86-87 us against 94-100 us
-// for 2 x 256 MiB at 4096 x 16384).
+// for 2 x 256 MiB at 4096 x 16384).  Held to 32 registers (8 CTAs per SM):
+// erf-GELU otherwise took 40 and ran at 6 CTAs per SM, 4 % slower in the
+// power-capped bench step; the other functions fit in 32 anyway.
 template <class F, int W>
-__global__ void __launch_bounds__(kThreads)
+__global__ void __launch_bounds__(kThreads, 8)
 elementwise_tile_kernel(const float* __restrict__ x, float* __restrict__ y, F f) {
   constexpr int U = kTile / (kThreads * W);
   const int64_t base = (int64_t)blockIdx.x * kTile + threadIdx.x * W;
